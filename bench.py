@@ -1,0 +1,578 @@
+"""Benchmark of the B200 reduce/scan path (BASELINE.json metric: achieved HBM
+GB/s for reduce/scan).
+
+Default workload: u32 exclusive prefix scan over
+2^28 elements per GPU, values h & 15 from seed 1 (SplitMix64 stream, generated
+on the device).  At N>1 GPUs every rank owns 2^28 elements of one global
+N*2^28-element buffer (weak scaling) and the step is the partitioned scan:
+local total -> NCCL all-gather of the totals -> carry -> seeded look-back scan.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                  [--config 1|2|3|4|5]
+
+Prints ONE JSON line on rank 0.  `value` is whole-job algorithmic bytes per
+second with inputs resident in HBM (CUDA events on the compute stream, max
+over ranks); `e2e` is the same metric through the public API with pinned host
+buffers and the host<->device copies inside the timed region; `roofline`
+compares the dominant kernel's algorithmic bytes per launch / its event-timed
+duration against the measured HBM copy bandwidth (MEASURED_PEAKS.json);
+`cpu_baseline` is the oracle restatement of the reference's host semantics
+timed on this box's cores on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "achieved HBM GB/s (and % of ~8 TB/s) for reduce/scan at 1/2/4/8 B200"
+L2_BYTES = 126 * 2**20
+
+CONFIGS = {
+    1: dict(workload="f32 full sum reduction over 2^20 elements, uniform[-1,1) seed 0 "
+                     "(64 rotating buffers, 256 MiB > L2)", n=1 << 20, dtype="f32",
+            kernel="reduce_dense_kernel", bytes_per_elem=4),
+    2: dict(workload="u32 exclusive prefix scan over 2^28 elements per GPU, h&15 seed 1",
+            n=1 << 28, dtype="u32", kernel="scan_lookback_kernel", bytes_per_elem=8),
+    3: dict(workload="f32 row-wise max + argmax over [65536 x 4096] row-major, N(0,1) seed 2, "
+                     "~1% injected exact ties", rows=65536, cols=4096, dtype="f32",
+            kernel="row_reduce_kernel"),
+    4: dict(workload="f64 column-wise (axis=0) sum over [4096 x 65536] row-major, U[0,1) seed 3",
+            rows=4096, cols=65536, dtype="f64", kernel="col_reduce_kernel"),
+    5: dict(workload="i32 inclusive scan + i64-accumulated sum over 2^32 elements (16 GiB) "
+                     "U{-1000..1000} seed 4, partitioned 1-D across the GPUs",
+            n=1 << 32, dtype="i32", kernel="scan_lookback_kernel"),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end measurement")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            p = json.load(fh)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic(kernel: str, config: int):
+    """dram bytes per launch recorded from an ncu capture (profiles/*.md line
+    `traffic[<config>] <kernel>: <bytes>`), or None."""
+    pat = re.compile(rf"traffic\[{config}\]\s+{re.escape(kernel)}:\s*([0-9.eE+]+)")
+    pdir = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(pdir):
+        return None
+    for f in sorted(os.listdir(pdir)):
+        if f.endswith((".md", ".txt")):
+            m = pat.search(open(os.path.join(pdir, f)).read())
+            if m:
+                return float(m.group(1))
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------- reference arm
+
+
+def cpu_sample(cfg_id: int, cfg: dict, oracle, seconds: float = 10.0, threads: int = 0):
+    """Time the oracle's multithreaded restatement on a bounded sample.
+    Returns (GB/s, cores, sample description)."""
+    cores = oracle.max_threads() if threads == 0 else threads
+    if cfg_id == 2 or cfg_id == 5:
+        n = 1 << 26
+        dt = np.uint32 if cfg_id == 2 else np.int32
+        kind = oracle.GEN_U32_LOW4 if cfg_id == 2 else oracle.GEN_I32_PM1000
+        x = oracle.generate(kind, 1 if cfg_id == 2 else 4, n)
+        out = np.empty_like(x)
+        fn = (oracle.exclusive_scan_u32_mt if cfg_id == 2 else oracle.inclusive_scan_i32_mt)
+        fn(x, out, 0, threads)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            fn(x, out, 0, threads)
+            reps += 1
+        dt_s = (time.perf_counter() - t0) / reps
+        return 8 * n / dt_s / 1e9, cores, f"{'exclusive u32' if cfg_id == 2 else 'inclusive i32'} " \
+                                          f"scan of 2^26 elements x {reps} reps"
+    if cfg_id == 1:
+        n = cfg["n"]
+        x = oracle.generate(oracle.GEN_F32_UNIFORM_PM1, 0, n)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            oracle.sum_f32_mt(x, threads)
+            reps += 1
+        return 4 * n / ((time.perf_counter() - t0) / reps) / 1e9, cores, f"f32 sum of 2^20 x {reps} reps"
+    if cfg_id == 3:
+        rows, cols = 8192, cfg["cols"]
+        x = oracle.generate(oracle.GEN_F32_NORMAL, 2, rows * cols)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            oracle.row_argmax_f32_mt(x, rows, cols, threads)
+            reps += 1
+        return (4 * rows * cols + 8 * rows) / ((time.perf_counter() - t0) / reps) / 1e9, cores, \
+            f"row max+argmax of [8192 x 4096] x {reps} reps"
+    rows, cols = 512, cfg["cols"]
+    x = oracle.generate(oracle.GEN_F64_UNIT, 3, rows * cols)
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        oracle.col_sum_f64_mt(x, rows, cols, threads)
+        reps += 1
+    return (8 * rows * cols + 8 * cols) / ((time.perf_counter() - t0) / reps) / 1e9, cores, \
+        f"column sum of [512 x 65536] f64 x {reps} reps"
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    sys.path.insert(0, ROOT)
+    from oracle import host_ref as oracle
+    oracle.build()
+    per_step = max(1.0, min(6.0, 120.0 / max(1, args.steps + args.warmup)))
+    vals = []
+    desc, cores = "", 0
+    for i in range(args.warmup + args.steps):
+        v, cores, desc = cpu_sample(args.config, cfg, oracle, seconds=per_step)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "weak" if args.config == 2 else "strong",
+        "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
+        "config": {"workload": cfg["workload"], "config_index": args.config},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": desc + " per step (oracle restatement of the host reference "
+                                          "semantics, OpenMP over all cores)"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------- b200 arm
+
+
+def main():
+    args = parse()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+
+    import torch
+    sys.path.insert(0, ROOT)
+    import hephaestus_b200 as H
+    import hephaestus_b200.seams as S
+    from hephaestus_b200.core import CumSumOp, Layout, StridedView, SumOp
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = H.CudaDevice(local)
+    stream = torch.cuda.Stream(device=local)
+    sp = stream.cuda_stream
+    peak, peak_kind = peaks()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    comm = None
+    if world > 1 and args.config in (2, 5):
+        from hephaestus_b200.dist import Communicator
+        comm = Communicator.from_torch(dev)
+
+    # ---------------- workload set-up (inputs generated on the device) -------------
+    launches_per_step = 1
+    e2e_fn = None
+    if args.config == 2:
+        n = cfg["n"]
+        x = dev.alloc_uninitialized(np.uint32, n)
+        S.synth_fill(dev, x, S.SYNTH_U32_LOW4, seed=1, index_base=rank * n, stream=sp)
+        y = dev.alloc_uninitialized(np.uint32, n)
+        lay = Layout.c_contiguous([n])
+        bytes_per_step = 8 * n
+        if comm:
+            def step():
+                comm.scan_into(CumSumOp, StridedView(x, lay), StridedView(y, lay), exclusive=True, stream=sp)
+            launches_per_step = 4  # reduce, fold, scan + (NCCL all-gather, not ours)
+        else:
+            ops = H.CudaScanOps()
+
+            def step():
+                ops.scan_axis_into(CumSumOp, dev, StridedView(x, lay), 0, 0, StridedView(y, lay),
+                                   exclusive=True, stream=sp)
+        kernel_bytes = 8 * n
+        kernel_step = None if not comm else (lambda: H.CudaScanOps().scan_axis_into(
+            CumSumOp, dev, StridedView(x, lay), 0, 0, StridedView(y, lay), exclusive=True, stream=sp))
+        units = n
+    elif args.config == 1:
+        n = cfg["n"]
+        nbuf = 64
+        bufs = []
+        for b in range(nbuf):
+            xb = dev.alloc_uninitialized(np.float32, n)
+            S.synth_fill(dev, xb, S.SYNTH_F32_UNIFORM_PM1, seed=0, stream=sp)
+            bufs.append(xb)
+        out = dev.alloc_zeroed(np.float32, nbuf)
+        lay = Layout.c_contiguous([n])
+        ops = H.CudaFullReductionOps()
+        ctr = [0]
+
+        def step():
+            b = ctr[0] % nbuf
+            ctr[0] += 1
+            ops.reduce_full_into(SumOp, dev, StridedView(bufs[b], lay),
+                                 StridedView(out, Layout.try_new([1], [1], b)), stream=sp)
+        bytes_per_step = 4 * n
+        kernel_bytes = 4 * n
+        kernel_step = None
+        units = n
+    elif args.config == 3:
+        rows, cols = cfg["rows"], cfg["cols"]
+        x = dev.alloc_uninitialized(np.float32, rows * cols)
+        S.synth_fill(dev, x, S.SYNTH_F32_NORMAL, seed=2, stream=sp)
+        S.synth_inject_row_ties(dev, x, rows, cols, seed=2, stream=sp)
+        vals = dev.alloc_zeroed(np.float32, rows)
+        idx = dev.alloc_zeroed(np.uint32, rows)
+        ops = H.CudaAxisReductionOps()
+        il, ol = Layout.c_contiguous([rows, cols]), Layout.c_contiguous([rows, 1])
+
+        def step():
+            ops.argmax_axis_into(dev, StridedView(x, il), 1, StridedView(vals, ol), StridedView(idx, ol),
+                                 stream=sp)
+        bytes_per_step = 4 * rows * cols + 8 * rows
+        kernel_bytes = bytes_per_step
+        kernel_step = None
+        units = rows * cols
+    elif args.config == 4:
+        rows, cols = cfg["rows"], cfg["cols"]
+        x = dev.alloc_uninitialized(np.float64, rows * cols)
+        S.synth_fill(dev, x, S.SYNTH_F64_UNIT, seed=3, stream=sp)
+        out = dev.alloc_zeroed(np.float64, cols)
+        ops = H.CudaAxisReductionOps()
+        il, ol = Layout.c_contiguous([rows, cols]), Layout.c_contiguous([1, cols])
+
+        def step():
+            ops.reduce_axis_into(SumOp, dev, StridedView(x, il), 0, StridedView(out, ol), stream=sp)
+        bytes_per_step = 8 * rows * cols + 8 * cols
+        kernel_bytes = bytes_per_step
+        launches_per_step = 2  # column slices + slice finalize
+        kernel_step = None
+        units = rows * cols
+    else:  # config 5: strong scaling of 2^32 i32 over the ranks
+        total = cfg["n"]
+        n = (total + world - 1) // world
+        n = min(n, total - rank * n)
+        x = dev.alloc_uninitialized(np.int32, n)
+        S.synth_fill(dev, x, S.SYNTH_I32_PM1000, seed=4, index_base=rank * ((total + world - 1) // world),
+                     stream=sp)
+        y = dev.alloc_uninitialized(np.int32, n)
+        s64 = dev.alloc_zeroed(np.int64, 1)
+        lay = Layout.c_contiguous([n])
+        one = Layout.c_contiguous([1])
+        if comm:
+            def step():
+                comm.scan_into(CumSumOp, StridedView(x, lay), StridedView(y, lay), stream=sp)
+                comm.reduce_full_into(SumOp, StridedView(x, lay), StridedView(s64, one), stream=sp)
+            launches_per_step = 7
+        else:
+            sops, fops = H.CudaScanOps(), H.CudaFullReductionOps()
+
+            def step():
+                sops.scan_axis_into(CumSumOp, dev, StridedView(x, lay), 0, 0, StridedView(y, lay), stream=sp)
+                fops.reduce_full_into(SumOp, dev, StridedView(x, lay), StridedView(s64, one), stream=sp)
+            launches_per_step = 2
+        bytes_per_step = 8 * n + 4 * n  # scan r+w, then the widening sum reads again
+        kernel_bytes = 8 * n
+        kernel_step = lambda: H.CudaScanOps().scan_axis_into(  # noqa: E731
+            CumSumOp, dev, StridedView(x, lay), 0, 0, StridedView(y, lay), stream=sp)
+        units = n
+    dev.synchronize_stream(sp)
+
+    # ---------------- warm-up, then exactly K timed steps -------------
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    dev.synchronize_stream(sp)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    with ClockSampler(local) as clocks:
+        time.sleep(0.3)
+        barrier()
+        t_all0 = torch.cuda.Event(enable_timing=True)
+        t_all1 = torch.cuda.Event(enable_timing=True)
+        t_all0.record(stream)
+        for k in range(args.steps):
+            starts[k].record(stream)
+            step()
+            ends[k].record(stream)
+        t_all1.record(stream)
+        dev.synchronize_stream(sp)
+        barrier()
+    total_ms_local = t_all0.elapsed_time(t_all1)
+    total_ms = max_over_ranks(total_ms_local)
+    per_launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms_per_step = total_ms / args.steps
+    value = bytes_per_step * world * args.steps / (total_ms / 1e3) / 1e9
+
+    # ---------------- dominant kernel roofline -------------
+    if kernel_step is not None:
+        ks, ke = [], []
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                kernel_step()
+            for _ in range(10):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                kernel_step()
+                b.record(stream)
+                ks.append(a)
+                ke.append(b)
+        dev.synchronize_stream(sp)
+        kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(ks, ke))
+    else:
+        kernel_ms = statistics.mean(per_launch_ms)
+    achieved = kernel_bytes / (kernel_ms / 1e3) / 1e9
+    traffic = profiled_traffic(cfg["kernel"], args.config)
+
+    # ---------------- end to end through the public API with host buffers -------------
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, cfg, dev, stream, sp, world, rank, comm, max_over_ranks, barrier)
+
+    # ---------------- CPU baseline (rank 0, N=1 only) -------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import host_ref as oracle
+        oracle.build()
+        v, cores, desc = cpu_sample(args.config, cfg, oracle, seconds=10.0)
+        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+               "sample": desc + " (oracle restatement of the host reference semantics, OpenMP)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6),
+            "higher_is_better": True, "scaling": "weak" if args.config in (1, 2, 3, 4) else "strong",
+            "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
+            "config": {"workload": cfg["workload"], "config_index": args.config,
+                       "elements_per_gpu": units,
+                       "elements_per_s": round(units * world / (ms_per_step / 1e3), 1),
+                       "fraction_of_hbm_peak": round(value / world / peak, 4),
+                       "l2": "inputs larger than L2" if args.config != 1 else
+                             "64 rotating 4 MiB inputs (256 MiB > L2)",
+                       "parallelism": f"partitioned1d{world}" if comm else
+                                      (f"replicas{world}" if world > 1 else "single")},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": cfg["kernel"], "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": kernel_bytes,
+                         "launch_ms": round(kernel_ms, 6)},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks.summary(),
+            "gpu_launches": launches_per_step * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if comm:
+        comm.destroy()
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(args, cfg, dev, stream, sp, world, rank, comm, max_over_ranks, barrier):
+    """Same metric through the public API: pinned host input uploaded, the path
+    run, the result read back, every step inside the timed region."""
+    import ctypes
+
+    import torch
+
+    import hephaestus_b200 as H
+    from hephaestus_b200 import _native as N
+    from hephaestus_b200.core import CumSumOp, Layout, StridedView, SumOp, check
+
+    def pinned(nbytes):
+        p = ctypes.c_void_p()
+        check(N.lib.heph_host_alloc_pinned(nbytes, ctypes.byref(p)))
+        return p
+
+    if args.config in (2, 5):
+        dt = np.uint32 if args.config == 2 else np.int32
+        total = cfg["n"]
+        n = total if args.config == 2 else min((total + world - 1) // world, total - rank * ((total + world - 1) // world))
+        es = 4
+        hin, hout = pinned(n * es), pinned(n * es)
+        x = dev.alloc_uninitialized(dt, n)
+        y = dev.alloc_uninitialized(dt, n)
+        lay = Layout.c_contiguous([n])
+        ops = H.CudaScanOps()
+
+        def e2e_step():
+            check(N.lib.heph_buffer_upload_async(dev.handle, x.handle, 0, hin, n, ctypes.c_void_p(sp)))
+            if comm:
+                comm.scan_into(CumSumOp, StridedView(x, lay), StridedView(y, lay), exclusive=args.config == 2,
+                               stream=sp)
+            else:
+                ops.scan_axis_into(CumSumOp, dev, StridedView(x, lay), 0, 0, StridedView(y, lay),
+                                   exclusive=args.config == 2, stream=sp)
+            check(N.lib.heph_buffer_download_async(dev.handle, y.handle, 0, hout, n, ctypes.c_void_p(sp)))
+        bytes_step = 8 * n
+        h2d, d2h = n * es, n * es
+    elif args.config == 1:
+        n = cfg["n"]
+        hin = pinned(4 * n)
+        hout = pinned(4)
+        x = dev.alloc_uninitialized(np.float32, n)
+        out = dev.alloc_zeroed(np.float32, 1)
+        lay = Layout.c_contiguous([n])
+        ops = H.CudaFullReductionOps()
+
+        def e2e_step():
+            check(N.lib.heph_buffer_upload_async(dev.handle, x.handle, 0, hin, n, ctypes.c_void_p(sp)))
+            ops.reduce_full_into(SumOp, dev, StridedView(x, lay), StridedView(out, Layout.c_contiguous([1])),
+                                 stream=sp)
+            check(N.lib.heph_buffer_download_async(dev.handle, out.handle, 0, hout, 1, ctypes.c_void_p(sp)))
+        bytes_step, h2d, d2h = 4 * n, 4 * n, 4
+    elif args.config == 3:
+        rows, cols = cfg["rows"], cfg["cols"]
+        hin, hv, hi = pinned(4 * rows * cols), pinned(4 * rows), pinned(4 * rows)
+        x = dev.alloc_uninitialized(np.float32, rows * cols)
+        vals, idx = dev.alloc_zeroed(np.float32, rows), dev.alloc_zeroed(np.uint32, rows)
+        ops = H.CudaAxisReductionOps()
+        il, ol = Layout.c_contiguous([rows, cols]), Layout.c_contiguous([rows, 1])
+
+        def e2e_step():
+            check(N.lib.heph_buffer_upload_async(dev.handle, x.handle, 0, hin, rows * cols, ctypes.c_void_p(sp)))
+            ops.argmax_axis_into(dev, StridedView(x, il), 1, StridedView(vals, ol), StridedView(idx, ol), stream=sp)
+            check(N.lib.heph_buffer_download_async(dev.handle, vals.handle, 0, hv, rows, ctypes.c_void_p(sp)))
+            check(N.lib.heph_buffer_download_async(dev.handle, idx.handle, 0, hi, rows, ctypes.c_void_p(sp)))
+        bytes_step, h2d, d2h = 4 * rows * cols + 8 * rows, 4 * rows * cols, 8 * rows
+    else:
+        rows, cols = cfg["rows"], cfg["cols"]
+        hin, ho = pinned(8 * rows * cols), pinned(8 * cols)
+        x = dev.alloc_uninitialized(np.float64, rows * cols)
+        out = dev.alloc_zeroed(np.float64, cols)
+        ops = H.CudaAxisReductionOps()
+        il, ol = Layout.c_contiguous([rows, cols]), Layout.c_contiguous([1, cols])
+
+        def e2e_step():
+            check(N.lib.heph_buffer_upload_async(dev.handle, x.handle, 0, hin, rows * cols, ctypes.c_void_p(sp)))
+            ops.reduce_axis_into(SumOp, dev, StridedView(x, il), 0, StridedView(out, ol), stream=sp)
+            check(N.lib.heph_buffer_download_async(dev.handle, out.handle, 0, ho, cols, ctypes.c_void_p(sp)))
+        bytes_step, h2d, d2h = 8 * rows * cols + 8 * cols, 8 * rows * cols, 8 * cols
+
+    steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    dev.synchronize_stream(sp)
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    b.record(stream)
+    dev.synchronize_stream(sp)
+    ms = max_over_ranks(a.elapsed_time(b)) / steps
+    return {"value": round(bytes_step * world / (ms / 1e3) / 1e9, 3), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4),
+            "steps": steps}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,252 @@
+// dist.cu — partitioned 1-D reduce and scan across the GPUs of one node, one
+// process per GPU, NCCL over NVLink/NVSwitch for the exchange.
+//
+// The reference has no multi-device path (hephaestus-cuda opens independent
+// contexts per ordinal, infrastructure/device.rs:657-672).  The exchange here
+// is a few bytes per rank, so the whole call stays stream-ordered with no host
+// synchronisation:
+//   reduce: local single-pass reduction -> ncclAllGather of the per-rank
+//           partials -> one thread folds them in rank order into `out`;
+//   scan:   local reduction of the slice (its total) -> ncclAllGather of the
+//           totals -> carry = fold of the lower ranks' totals -> look-back
+//           scan of the slice seeded with the carry.
+// NCCL is resolved at run time from the libnccl.so.2 already loaded into the
+// process (torch's), else from the loader path, so this library carries no
+// link-time NCCL dependency.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "plan.h"
+
+namespace heph {
+namespace {
+
+struct NcclApi {
+    bool loaded = false;
+    std::string why;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+    const char *(*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi &nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            const char *e = dlerror();
+            api.why = std::string("libnccl.so.2 could not be loaded: ") + (e ? e : "unknown");
+            return;
+        }
+        auto sym = [&](const char *name) { return dlsym(h, name); };
+        api.GetUniqueId = (decltype(api.GetUniqueId))sym("ncclGetUniqueId");
+        api.CommInitRank = (decltype(api.CommInitRank))sym("ncclCommInitRank");
+        api.AllGather = (decltype(api.AllGather))sym("ncclAllGather");
+        api.CommDestroy = (decltype(api.CommDestroy))sym("ncclCommDestroy");
+        api.CommAbort = (decltype(api.CommAbort))sym("ncclCommAbort");
+        api.CommGetAsyncError = (decltype(api.CommGetAsyncError))sym("ncclCommGetAsyncError");
+        api.GetErrorString = (decltype(api.GetErrorString))sym("ncclGetErrorString");
+        api.loaded = api.GetUniqueId && api.CommInitRank && api.AllGather && api.CommDestroy &&
+                     api.CommAbort && api.GetErrorString;
+        if (!api.loaded) api.why = "libnccl.so.2 lacks a required symbol";
+    });
+    return api;
+}
+
+heph_status nccl_fail(ncclResult_t r, const char *what) {
+    const char *s = nccl().GetErrorString ? nccl().GetErrorString(r) : "unknown";
+    return fail(HEPH_DISPATCH_FAILED, std::string(what) + ": " + s);
+}
+
+template <typename T, int OP>
+__global__ void fold_ranks_kernel(const T *__restrict__ gathered, int count, T *__restrict__ out) {
+    T acc = identity<T, OP>();
+    for (int r = 0; r < count; ++r) acc = combine<T, OP>(acc, gathered[r]);
+    *out = acc;
+}
+
+template <typename T>
+heph_status launch_fold(cudaStream_t s, int op, const void *g, int count, void *out) {
+    const T *tg = static_cast<const T *>(g);
+    T *to = static_cast<T *>(out);
+    switch (op) {
+        case OP_SUM: fold_ranks_kernel<T, OP_SUM><<<1, 1, 0, s>>>(tg, count, to); break;
+        case OP_PROD: fold_ranks_kernel<T, OP_PROD><<<1, 1, 0, s>>>(tg, count, to); break;
+        case OP_MIN: fold_ranks_kernel<T, OP_MIN><<<1, 1, 0, s>>>(tg, count, to); break;
+        case OP_MAX: fold_ranks_kernel<T, OP_MAX><<<1, 1, 0, s>>>(tg, count, to); break;
+        default: return fail(HEPH_INVALID_CONFIGURATION, "unknown operator");
+    }
+    HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "rank fold launch");
+    return HEPH_OK;
+}
+
+}  // namespace
+}  // namespace heph
+
+using namespace heph;
+
+struct heph_comm {
+    Device *device = nullptr;
+    ncclComm_t nccl = nullptr;
+    int nranks = 0, rank = 0;
+    void *scratch = nullptr;  // [total: 8 B][carry: 8 B][gathered: 8 B x nranks]
+    bool aborted = false;
+};
+
+extern "C" heph_status heph_comm_unique_id(uint8_t id[HEPH_COMM_ID_BYTES]) {
+    static_assert(sizeof(ncclUniqueId) == HEPH_COMM_ID_BYTES, "NCCL id size");
+    NcclApi &api = nccl();
+    if (!api.loaded) return fail(HEPH_ADAPTER_UNAVAILABLE, api.why);
+    ncclUniqueId uid;
+    ncclResult_t r = api.GetUniqueId(&uid);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+    std::memcpy(id, &uid, sizeof(uid));
+    return HEPH_OK;
+}
+
+extern "C" heph_status heph_comm_init(heph_device *device, const uint8_t id[HEPH_COMM_ID_BYTES],
+                                      int nranks, int rank, heph_comm **out) {
+    if (!device || !id || !out) return fail(HEPH_INVALID_CONFIGURATION, "null argument");
+    *out = nullptr;
+    if (nranks < 1 || rank < 0 || rank >= nranks)
+        return fail(HEPH_INVALID_CONFIGURATION, "rank " + std::to_string(rank) + " of " +
+                                                    std::to_string(nranks) + " is invalid");
+    NcclApi &api = nccl();
+    if (!api.loaded) return fail(HEPH_ADAPTER_UNAVAILABLE, api.why);
+    Device *dev = reinterpret_cast<Device *>(device);
+    heph_status st = bind(dev);
+    if (st != HEPH_OK) return st;
+    heph_comm *c = new heph_comm();
+    c->device = dev;
+    c->nranks = nranks;
+    c->rank = rank;
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    ncclResult_t r = api.CommInitRank(&c->nccl, nranks, uid, rank);
+    if (r != ncclSuccess) {
+        delete c;
+        return nccl_fail(r, "ncclCommInitRank");
+    }
+    if (cudaMalloc(&c->scratch, 16 + 8 * (size_t)nranks) != cudaSuccess) {
+        cudaGetLastError();
+        api.CommDestroy(c->nccl);
+        delete c;
+        return fail(HEPH_ALLOCATION_FAILED, "communicator scratch allocation failed");
+    }
+    *out = c;
+    return HEPH_OK;
+}
+
+extern "C" heph_status heph_comm_destroy(heph_comm *comm) {
+    if (!comm) return HEPH_OK;
+    cudaSetDevice(comm->device->ordinal);
+    if (comm->nccl && !comm->aborted) nccl().CommDestroy(comm->nccl);
+    if (comm->scratch) cudaFree(comm->scratch);
+    delete comm;
+    return HEPH_OK;
+}
+
+extern "C" heph_status heph_comm_abort(heph_comm *comm) {
+    if (!comm) return HEPH_OK;
+    if (comm->nccl && !comm->aborted) {
+        nccl().CommAbort(comm->nccl);
+        comm->aborted = true;
+    }
+    return HEPH_OK;
+}
+
+static heph_status partitioned_args(heph_comm *comm, const heph_buffer *in, const heph_layout *il,
+                                    const heph_buffer *out, const heph_layout *ol) {
+    if (!comm || !in || !il || !out || !ol) return fail(HEPH_INVALID_CONFIGURATION, "null argument");
+    if (comm->aborted) return fail(HEPH_DISPATCH_FAILED, "communicator was aborted");
+    const Buffer *bi = reinterpret_cast<const Buffer *>(in);
+    const Buffer *bo = reinterpret_cast<const Buffer *>(out);
+    if (bi->device != comm->device || bo->device != comm->device)
+        return fail(HEPH_DISPATCH_FAILED, "operand buffers belong to another device");
+    if (il->rank != 1) return fail(HEPH_DISPATCH_FAILED, "partitioned operands are rank-1 slices");
+    return HEPH_OK;
+}
+
+extern "C" heph_status heph_partitioned_reduce_full(heph_comm *comm, heph_op op,
+                                                    const heph_buffer *in, const heph_layout *in_layout,
+                                                    heph_buffer *out, const heph_layout *out_layout,
+                                                    heph_stream stream) {
+    heph_status st = partitioned_args(comm, in, in_layout, out, out_layout);
+    if (st != HEPH_OK) return st;
+    const Buffer *bi = reinterpret_cast<const Buffer *>(in);
+    Buffer *bo = reinterpret_cast<Buffer *>(out);
+    if (op != HEPH_SUM && op != HEPH_PROD && op != HEPH_MIN && op != HEPH_MAX)
+        return fail(HEPH_INVALID_CONFIGURATION, "full reduction supports sum, prod, min and max");
+    const bool widen = (bi->dtype == HEPH_I32 && bo->dtype == HEPH_I64) ||
+                       (bi->dtype == HEPH_F32 && bo->dtype == HEPH_F64);
+    if (bi->dtype != bo->dtype && !widen)
+        return fail(HEPH_DISPATCH_FAILED, "full reduction output element type must match the input or widen it");
+    uint64_t count = 0;
+    st = plan_full_reduction(*in_layout, bi->len, *out_layout, bo->len, &count);
+    if (st != HEPH_OK) return st;
+    Device *dev = comm->device;
+    st = bind(dev);
+    if (st != HEPH_OK) return st;
+    cudaStream_t s = resolve_stream(dev, stream);
+    char *scratch = static_cast<char *>(comm->scratch);
+    st = launch_reduce_full(dev, s, op, bi->dtype, bo->dtype, bi->ptr, *in_layout, count, scratch);
+    if (st != HEPH_OK) return st;
+    const size_t es = dtype_size(bo->dtype);
+    ncclResult_t r = nccl().AllGather(scratch, scratch + 16, es, ncclUint8, comm->nccl, s);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
+    void *dst = static_cast<char *>(bo->ptr) + out_layout->offset * es;
+    return dispatch_dtype(bo->dtype, [&]<typename T>() {
+        return launch_fold<T>(s, op, scratch + 16, comm->nranks, dst);
+    });
+}
+
+extern "C" heph_status heph_partitioned_scan(heph_comm *comm, heph_op op, int exclusive,
+                                             const heph_buffer *in, const heph_layout *in_layout,
+                                             heph_buffer *out, const heph_layout *out_layout,
+                                             heph_stream stream) {
+    heph_status st = partitioned_args(comm, in, in_layout, out, out_layout);
+    if (st != HEPH_OK) return st;
+    const Buffer *bi = reinterpret_cast<const Buffer *>(in);
+    Buffer *bo = reinterpret_cast<Buffer *>(out);
+    if (op != HEPH_SUM && op != HEPH_PROD)
+        return fail(HEPH_INVALID_CONFIGURATION, "scans support the sum (cumsum) and product (cumprod) operators");
+    if (bi->dtype != bo->dtype) return fail(HEPH_DISPATCH_FAILED, "scan output element type must match the input");
+    bool noop = false;
+    AxisProblem p;
+    const bool alias = bi->ptr == bo->ptr;
+    st = plan_axis_scan(*in_layout, bi->len, *out_layout, bo->len, 0, alias, &noop, &p);
+    if (st != HEPH_OK) return st;
+    Device *dev = comm->device;
+    st = bind(dev);
+    if (st != HEPH_OK) return st;
+    cudaStream_t s = resolve_stream(dev, stream);
+    char *scratch = static_cast<char *>(comm->scratch);
+    const size_t es = dtype_size(bi->dtype);
+    // 1. total of the local slice (the identity for an empty slice).
+    st = launch_reduce_full(dev, s, op, bi->dtype, bi->dtype, bi->ptr, *in_layout, noop ? 0 : p.len, scratch);
+    if (st != HEPH_OK) return st;
+    // 2. every rank's total.
+    ncclResult_t r = nccl().AllGather(scratch, scratch + 16, es, ncclUint8, comm->nccl, s);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
+    // 3. carry = fold of the totals of the lower ranks.
+    st = dispatch_dtype(bi->dtype, [&]<typename T>() {
+        return launch_fold<T>(s, op, scratch + 16, comm->rank, scratch + 8);
+    });
+    if (st != HEPH_OK) return st;
+    if (noop) return HEPH_OK;
+    // 4. single-pass scan of the slice seeded with the carry.
+    return launch_scan(dev, s, op, bi->dtype, bi->ptr, bo->ptr, p, false, exclusive != 0, scratch + 8);
+}

@@ -1,0 +1,31 @@
+// kernels.h — host launchers of the sm_100a kernels (one per kernel family).
+// Each launcher validates nothing (the C ABI layer has planned the call) and
+// enqueues on `stream`; workspaces come from the device's per-stream pool.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "plan.h"
+
+namespace heph {
+
+// Full reduction of `count` elements of the view (base pointer = buffer
+// start, layout in elements) into the single element at `out`.
+// acc_dtype == in_dtype, or a widening pair (I32->I64, F32->F64).
+heph_status launch_reduce_full(Device *dev, cudaStream_t stream, int op, heph_dtype in_dtype,
+                               heph_dtype acc_dtype, const void *base, const heph_layout &layout,
+                               uint64_t count, void *out);
+
+// Rank-2 axis reduction.  `mean` divides the sum by the axis length;
+// `indices` (u32, same layout as out) selects the arg-reduction form.
+heph_status launch_reduce_axis(Device *dev, cudaStream_t stream, int op, heph_dtype dtype,
+                               const void *in, const AxisProblem &p, void *out, bool mean,
+                               uint32_t *indices, int64_t idx_base, int64_t idx_o);
+
+// Axis scan (rank 1 or 2).  `carry` (nullable, device) seeds line 0.
+heph_status launch_scan(Device *dev, cudaStream_t stream, int op, heph_dtype dtype,
+                        const void *in, void *out, const AxisProblem &p, bool reverse,
+                        bool exclusive, const void *carry);
+
+}  // namespace heph

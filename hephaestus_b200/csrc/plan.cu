@@ -1,0 +1,263 @@
+// plan.cpp — validation and planning (host only; no CUDA calls).
+//
+// Follows the reference planners message for message:
+//   plan_axis_reduction  crates/hephaestus-core/src/domain/reduction.rs:410-500
+//   plan_axis_scan       crates/hephaestus-core/src/domain/scan.rs:87-178
+//   full reduction       crates/hephaestus-cuda/src/application/full_reduction_seam.rs:59-72
+//   layout errors        crates/hephaestus-core/src/domain/planning.rs:10-14 ("layout rejected: ")
+// Extents, strides and offsets are 64-bit, so the u32/i32 narrowing errors of
+// the reference (planning.rs:17-28) do not arise.
+#include "plan.h"
+
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace heph {
+
+std::string shape_debug(const heph_layout &l) {
+    std::string s = "[";
+    for (uint32_t d = 0; d < l.rank && d < HEPH_MAX_RANK; ++d) {
+        if (d) s += ", ";
+        s += std::to_string(l.shape[d]);
+    }
+    return s + "]";
+}
+
+bool layout_size(const heph_layout &l, uint64_t *out) {
+    unsigned __int128 n = 1;
+    for (uint32_t d = 0; d < l.rank; ++d) {
+        n *= l.shape[d];
+        if (n > (unsigned __int128)UINT64_MAX) return false;
+    }
+    *out = (uint64_t)n;
+    return true;
+}
+
+bool layout_fits(const heph_layout &l, uint64_t buffer_len, std::string *why) {
+    if (l.rank < 1 || l.rank > HEPH_MAX_RANK) {
+        *why = "rank " + std::to_string(l.rank) + " is outside 1..=" + std::to_string(HEPH_MAX_RANK);
+        return false;
+    }
+    uint64_t size = 0;
+    if (!layout_size(l, &size)) {
+        *why = "element count of shape " + shape_debug(l) + " overflows";
+        return false;
+    }
+    if (size == 0) return true;
+    __int128 lo = (__int128)l.offset, hi = (__int128)l.offset;
+    for (uint32_t d = 0; d < l.rank; ++d) {
+        __int128 span = (__int128)(l.shape[d] - 1) * (__int128)l.strides[d];
+        if (span < 0) lo += span;
+        else hi += span;
+    }
+    if (lo < 0) {
+        *why = "shape " + shape_debug(l) + " with offset " + std::to_string(l.offset) +
+               " reaches below storage index 0";
+        return false;
+    }
+    if (hi >= (__int128)buffer_len) {
+        *why = "shape " + shape_debug(l) + " with offset " + std::to_string(l.offset) +
+               " needs storage index " + std::to_string((unsigned long long)hi) +
+               " but the buffer holds " + std::to_string(buffer_len) + " elements";
+        return false;
+    }
+    return true;
+}
+
+heph_status validate_layout(const heph_layout &l, uint64_t buffer_len) {
+    std::string why;
+    if (!layout_fits(l, buffer_len, &why)) return fail(HEPH_DISPATCH_FAILED, "layout rejected: " + why);
+    return HEPH_OK;
+}
+
+bool has_zero_stride_aliasing(const heph_layout &l) {
+    for (uint32_t d = 0; d < l.rank; ++d)
+        if (l.shape[d] > 1 && l.strides[d] == 0) return true;
+    return false;
+}
+
+bool layout_is_dense(const heph_layout &l) {
+    int64_t expect = 1;
+    for (int d = (int)l.rank - 1; d >= 0; --d) {
+        if (l.shape[d] != 1 && l.strides[d] != expect) return false;
+        expect *= (int64_t)l.shape[d];
+    }
+    return true;
+}
+
+static bool same_shape(const heph_layout &a, const heph_layout &b) {
+    if (a.rank != b.rank) return false;
+    for (uint32_t d = 0; d < a.rank; ++d)
+        if (a.shape[d] != b.shape[d]) return false;
+    return true;
+}
+
+heph_status plan_axis_reduction(const heph_layout &in, uint64_t in_len, const heph_layout &out,
+                                uint64_t out_len, uint32_t axis, bool alias, bool *noop,
+                                AxisProblem *p) {
+    *noop = false;
+    if (axis >= 2)
+        return fail(HEPH_DISPATCH_FAILED,
+                    "axis " + std::to_string(axis) + " is out of bounds for rank-2 reduction");
+    if (in.rank != 2 || out.rank != 2)
+        return fail(HEPH_DISPATCH_FAILED, "axis reduction operands must be rank 2, got input rank " +
+                                              std::to_string(in.rank) + " and output rank " +
+                                              std::to_string(out.rank));
+    heph_layout expected = in;
+    expected.shape[axis] = 1;
+    if (!same_shape(expected, out))
+        return fail(HEPH_DISPATCH_FAILED, "axis reduction output shape mismatch: input " +
+                                              shape_debug(in) + ", axis " + std::to_string(axis) +
+                                              ", out " + shape_debug(out));
+    if (alias)
+        return fail(HEPH_DISPATCH_FAILED, "axis reduction output buffer must not alias input buffer");
+    if (has_zero_stride_aliasing(out))
+        return fail(HEPH_DISPATCH_FAILED,
+                    "axis reduction output layout must not contain zero-stride aliasing");
+    heph_status st = validate_layout(in, in_len);
+    if (st != HEPH_OK) return st;
+    st = validate_layout(out, out_len);
+    if (st != HEPH_OK) return st;
+    uint64_t out_size = 0;
+    layout_size(out, &out_size);
+    if (out_size == 0) {
+        *noop = true;
+        return HEPH_OK;
+    }
+    uint32_t other = 1 - axis;
+    p->outer = in.shape[other];
+    p->len = in.shape[axis];
+    p->in_base = (int64_t)in.offset;
+    p->in_o = in.strides[other];
+    p->in_r = in.strides[axis];
+    p->out_base = (int64_t)out.offset;
+    p->out_o = out.strides[other];
+    p->out_r = 0;
+    return HEPH_OK;
+}
+
+heph_status plan_axis_scan(const heph_layout &in, uint64_t in_len, const heph_layout &out,
+                           uint64_t out_len, uint32_t axis, bool alias, bool *noop,
+                           AxisProblem *p) {
+    *noop = false;
+    if (in.rank != 1 && in.rank != 2)
+        return fail(HEPH_DISPATCH_FAILED,
+                    "cuda-sm100a scan supports rank 1 or 2, got rank " + std::to_string(in.rank));
+    if (axis >= in.rank)
+        return fail(HEPH_DISPATCH_FAILED, "scan axis " + std::to_string(axis) +
+                                              " is out of bounds for rank-" +
+                                              std::to_string(in.rank) + " scan");
+    if (!same_shape(in, out))
+        return fail(HEPH_DISPATCH_FAILED, "scan output shape mismatch: input " + shape_debug(in) +
+                                              ", out " + shape_debug(out));
+    if (alias) return fail(HEPH_DISPATCH_FAILED, "scan output buffer must not alias input buffer");
+    if (has_zero_stride_aliasing(out))
+        return fail(HEPH_DISPATCH_FAILED, "scan output layout must not contain zero-stride aliasing");
+    heph_status st = validate_layout(in, in_len);
+    if (st != HEPH_OK) return st;
+    st = validate_layout(out, out_len);
+    if (st != HEPH_OK) return st;
+    uint64_t size = 0;
+    layout_size(out, &size);
+    if (size == 0) {
+        *noop = true;
+        return HEPH_OK;
+    }
+    p->in_base = (int64_t)in.offset;
+    p->out_base = (int64_t)out.offset;
+    p->len = in.shape[axis];
+    p->in_r = in.strides[axis];
+    p->out_r = out.strides[axis];
+    if (in.rank == 1) {
+        p->outer = 1;
+        p->in_o = 0;
+        p->out_o = 0;
+    } else {
+        uint32_t other = 1 - axis;
+        p->outer = in.shape[other];
+        p->in_o = in.strides[other];
+        p->out_o = out.strides[other];
+    }
+    return HEPH_OK;
+}
+
+heph_status plan_full_reduction(const heph_layout &in, uint64_t in_len, const heph_layout &out,
+                                uint64_t out_len, uint64_t *count) {
+    heph_status st = validate_layout(out, out_len);
+    if (st != HEPH_OK) return st;
+    uint64_t out_size = 0;
+    layout_size(out, &out_size);
+    if (out_size != 1)
+        return fail(HEPH_DISPATCH_FAILED, "full reduction output must have exactly 1 element");
+    if (!layout_size(in, count))
+        return fail(HEPH_DISPATCH_FAILED, "layout rejected: element count of shape " +
+                                              shape_debug(in) + " overflows");
+    return validate_layout(in, in_len);
+}
+
+}  // namespace heph
+
+// ------------------------------------------------------------------ C ABI
+
+using namespace heph;
+
+extern "C" heph_status heph_validate_reduction_width(uint32_t width) {
+    if (width == 0 || (width & (width - 1)) != 0)
+        return fail(HEPH_DISPATCH_FAILED,
+                    "reduction block width " + std::to_string(width) + " must be a power of two");
+    return HEPH_OK;
+}
+
+extern "C" heph_status heph_validate_scan_width(uint32_t width) {
+    if (width == 0 || (width & (width - 1)) != 0)
+        return fail(HEPH_DISPATCH_FAILED,
+                    "scan block width " + std::to_string(width) + " must be a power of two");
+    return HEPH_OK;
+}
+
+extern "C" uint64_t heph_reduction_pass_count(uint64_t len, uint32_t width) {
+    if (width < 2) return 0;
+    uint64_t passes = 0;
+    while (len > 1) {
+        len = (len + width - 1) / width;
+        ++passes;
+    }
+    return passes;
+}
+
+extern "C" heph_status heph_layout_validate(const heph_layout *layout, uint64_t buffer_len) {
+    if (!layout) return fail(HEPH_INVALID_CONFIGURATION, "layout is null");
+    return validate_layout(*layout, buffer_len);
+}
+
+extern "C" heph_status heph_plan_axis_reduction(const heph_layout *input, uint64_t input_len,
+                                                const heph_layout *output, uint64_t output_len,
+                                                uint32_t axis, int buffers_alias, int *out_noop) {
+    if (!input || !output) return fail(HEPH_INVALID_CONFIGURATION, "layout is null");
+    bool noop = false;
+    AxisProblem p;
+    heph_status st = plan_axis_reduction(*input, input_len, *output, output_len, axis,
+                                         buffers_alias != 0, &noop, &p);
+    if (out_noop) *out_noop = noop ? 1 : 0;
+    return st;
+}
+
+extern "C" heph_status heph_plan_axis_scan(const heph_layout *input, uint64_t input_len,
+                                           const heph_layout *output, uint64_t output_len,
+                                           uint32_t axis, int buffers_alias, int *out_noop) {
+    if (!input || !output) return fail(HEPH_INVALID_CONFIGURATION, "layout is null");
+    bool noop = false;
+    AxisProblem p;
+    heph_status st = plan_axis_scan(*input, input_len, *output, output_len, axis,
+                                    buffers_alias != 0, &noop, &p);
+    if (out_noop) *out_noop = noop ? 1 : 0;
+    return st;
+}
+
+extern "C" heph_status heph_plan_full_reduction(const heph_layout *input, uint64_t input_len,
+                                                const heph_layout *output, uint64_t output_len) {
+    if (!input || !output) return fail(HEPH_INVALID_CONFIGURATION, "layout is null");
+    uint64_t count = 0;
+    return plan_full_reduction(*input, input_len, *output, output_len, &count);
+}

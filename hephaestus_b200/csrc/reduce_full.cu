@@ -1,0 +1,200 @@
+// reduce_full.cu — single-kernel full reductions for sm_100a.
+//
+// Replaces the reference's multi-pass tree (hephaestus-cuda
+// application/reduction.rs:19-64 + prepared_reduction.rs:38-128, one launch
+// per 256-way level, a strided staging copy before it and a D2H/H2D scalar
+// round trip after it, full_reduction_seam.rs:96-114) with ONE launch:
+//   * dense views: grid-stride over 128-bit streaming loads, 4 vectors in
+//     flight per thread, grid = resident CTAs of all SMs;
+//   * warp fold with redux.sync (32-bit integer add/min/max) or xor-shuffles,
+//     then a shared-memory fold of the warp results;
+//   * per-CTA partial to the stream's workspace, atomic ticket, and the last
+//     CTA folds the partials in CTA order and writes the scalar in place.
+// Non-dense views (transposed, diagonal, negative strides; rank <= 4) take a
+// grid-stride kernel that decodes each logical index with the view's strides
+// and feeds the same fold/finalize.
+#include <algorithm>
+
+#include "device_utils.cuh"
+#include "kernels.h"
+
+namespace heph {
+
+constexpr int kReduceThreads = 256;
+constexpr int kReduceUnroll = 4;
+
+template <typename Tin, typename Tacc, int OP>
+__device__ __forceinline__ Tacc fold_vec(Tacc acc, uint4 raw) {
+    Vec16<Tin> v = as_elems<Tin>(raw);
+#pragma unroll
+    for (int c = 0; c < Vec16<Tin>::V; ++c) acc = combine<Tacc, OP>(acc, (Tacc)v.e[c]);
+    return acc;
+}
+
+// Folds the block's value into the output: per-CTA partial, ticket, last
+// CTA folds all partials in CTA order.
+template <typename Tacc, int OP>
+__device__ __forceinline__ void finish_grid(Tacc acc, Tacc *out, Tacc *partials,
+                                            unsigned int *ticket, Tacc *scratch) {
+    acc = block_fold<Tacc, OP, kReduceThreads>(acc, scratch);
+    if (gridDim.x == 1) {
+        if (threadIdx.x == 0) *out = acc;
+        return;
+    }
+    __shared__ bool am_last;
+    if (threadIdx.x == 0) {
+        partials[blockIdx.x] = acc;
+        __threadfence();
+        unsigned int t = atomicAdd(ticket, 1u);
+        am_last = (t == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!am_last) return;
+    __threadfence();
+    Tacc a = identity<Tacc, OP>();
+    for (unsigned int j = threadIdx.x; j < gridDim.x; j += kReduceThreads)
+        a = combine<Tacc, OP>(a, ld_cg(partials + j));
+    a = block_fold<Tacc, OP, kReduceThreads>(a, scratch);
+    if (threadIdx.x == 0) {
+        *out = a;
+        *ticket = 0u;  // leave the ticket at rest for the next launch
+    }
+}
+
+template <typename Tin, typename Tacc, int OP>
+__global__ void __launch_bounds__(kReduceThreads)
+    reduce_dense_kernel(const Tin *__restrict__ in, uint64_t n, Tacc *__restrict__ out,
+                        Tacc *__restrict__ partials, unsigned int *__restrict__ ticket) {
+    __shared__ Tacc scratch[kReduceThreads / 32];
+    constexpr int V = Vec16<Tin>::V;
+    const uint64_t tid = (uint64_t)blockIdx.x * kReduceThreads + threadIdx.x;
+    const uint64_t stride = (uint64_t)gridDim.x * kReduceThreads;
+
+    // Elements before the first 16-byte boundary and after the last one.
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(in);
+    uint64_t head = ((16u - (addr & 15u)) & 15u) / sizeof(Tin);
+    if (head > n) head = n;
+    const uint64_t nvec = (n - head) / V;
+    const uint64_t tail = head + nvec * V;
+    const uint4 *vin = reinterpret_cast<const uint4 *>(in + head);
+
+    Tacc acc = identity<Tacc, OP>();
+    uint64_t i = tid;
+    for (; i + (kReduceUnroll - 1) * stride < nvec; i += kReduceUnroll * stride) {
+        uint4 r[kReduceUnroll];
+#pragma unroll
+        for (int u = 0; u < kReduceUnroll; ++u) r[u] = ld_stream(vin + i + u * stride);
+#pragma unroll
+        for (int u = 0; u < kReduceUnroll; ++u) acc = fold_vec<Tin, Tacc, OP>(acc, r[u]);
+    }
+    for (; i < nvec; i += stride) acc = fold_vec<Tin, Tacc, OP>(acc, ld_stream(vin + i));
+    if (tid < head) acc = combine<Tacc, OP>(acc, (Tacc)in[tid]);
+    if (tid < n - tail) acc = combine<Tacc, OP>(acc, (Tacc)in[tail + tid]);
+
+    finish_grid<Tacc, OP>(acc, out, partials, ticket, scratch);
+}
+
+struct StridedView4 {
+    uint32_t rank;
+    uint64_t shape[HEPH_MAX_RANK];
+    int64_t strides[HEPH_MAX_RANK];
+    int64_t offset;
+};
+
+template <typename Tin, typename Tacc, int OP>
+__global__ void __launch_bounds__(kReduceThreads)
+    reduce_strided_kernel(const Tin *__restrict__ base, StridedView4 v, uint64_t n,
+                          Tacc *__restrict__ out, Tacc *__restrict__ partials,
+                          unsigned int *__restrict__ ticket) {
+    __shared__ Tacc scratch[kReduceThreads / 32];
+    Tacc acc = identity<Tacc, OP>();
+    const uint64_t stride = (uint64_t)gridDim.x * kReduceThreads;
+    for (uint64_t i = (uint64_t)blockIdx.x * kReduceThreads + threadIdx.x; i < n; i += stride) {
+        uint64_t rem = i;
+        int64_t off = v.offset;
+        for (int d = (int)v.rank - 1; d >= 0; --d) {
+            uint64_t c = rem % v.shape[d];
+            rem /= v.shape[d];
+            off += (int64_t)c * v.strides[d];
+        }
+        acc = combine<Tacc, OP>(acc, (Tacc)base[off]);
+    }
+    finish_grid<Tacc, OP>(acc, out, partials, ticket, scratch);
+}
+
+template <typename Tacc, int OP> __global__ void write_identity_kernel(Tacc *out) {
+    *out = identity<Tacc, OP>();
+}
+
+// ------------------------------------------------------------------ launch
+
+template <typename Tin, typename Tacc, int OP>
+static heph_status launch_typed(Device *dev, cudaStream_t stream, const void *base_v,
+                                const heph_layout &l, uint64_t count, void *out_v) {
+    const Tin *base = static_cast<const Tin *>(base_v);
+    Tacc *out = static_cast<Tacc *>(out_v);
+    if (count == 0) {
+        write_identity_kernel<Tacc, OP><<<1, 1, 0, stream>>>(out);
+        HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "full reduction launch");
+        return HEPH_OK;
+    }
+    const bool dense = layout_is_dense(l);
+    // Work per CTA: at least kReduceUnroll vectors per thread before adding CTAs.
+    const uint64_t per_cta = (uint64_t)kReduceThreads * kReduceUnroll * (16 / sizeof(Tin));
+    uint64_t want = (count + per_cta - 1) / per_cta;
+    const uint64_t cap = (uint64_t)dev->sm_count * (2048 / kReduceThreads);
+    unsigned int grid = (unsigned int)std::max<uint64_t>(1, std::min(want, cap));
+
+    std::lock_guard<std::mutex> lock(dev->mu);
+    Workspace *ws = nullptr;
+    heph_status st = workspace_for(dev, stream, (size_t)grid * sizeof(Tacc), 0, &ws);
+    if (st != HEPH_OK) return st;
+    Tacc *partials = static_cast<Tacc *>(ws->partials);
+    if (dense) {
+        reduce_dense_kernel<Tin, Tacc, OP><<<grid, kReduceThreads, 0, stream>>>(
+            base + l.offset, count, out, partials, ws->tickets);
+    } else {
+        StridedView4 v{};
+        v.rank = l.rank;
+        for (uint32_t d = 0; d < l.rank; ++d) {
+            v.shape[d] = l.shape[d];
+            v.strides[d] = l.strides[d];
+        }
+        v.offset = (int64_t)l.offset;
+        reduce_strided_kernel<Tin, Tacc, OP>
+            <<<grid, kReduceThreads, 0, stream>>>(base, v, count, out, partials, ws->tickets);
+    }
+    HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "full reduction launch");
+    return HEPH_OK;
+}
+
+template <typename Tin, typename Tacc>
+static heph_status launch_op(Device *dev, cudaStream_t stream, int op, const void *base,
+                             const heph_layout &l, uint64_t count, void *out) {
+    switch (op) {
+        case OP_SUM: return launch_typed<Tin, Tacc, OP_SUM>(dev, stream, base, l, count, out);
+        case OP_PROD: return launch_typed<Tin, Tacc, OP_PROD>(dev, stream, base, l, count, out);
+        case OP_MIN: return launch_typed<Tin, Tacc, OP_MIN>(dev, stream, base, l, count, out);
+        case OP_MAX: return launch_typed<Tin, Tacc, OP_MAX>(dev, stream, base, l, count, out);
+    }
+    return fail(HEPH_INVALID_CONFIGURATION, "full reduction supports sum, prod, min and max");
+}
+
+heph_status launch_reduce_full(Device *dev, cudaStream_t stream, int op, heph_dtype in_dtype,
+                               heph_dtype acc_dtype, const void *base, const heph_layout &l,
+                               uint64_t count, void *out) {
+    if (in_dtype == acc_dtype) {
+        return dispatch_dtype(in_dtype, [&]<typename T>() {
+            return launch_op<T, T>(dev, stream, op, base, l, count, out);
+        });
+    }
+    if (in_dtype == HEPH_I32 && acc_dtype == HEPH_I64)
+        return launch_op<int32_t, int64_t>(dev, stream, op, base, l, count, out);
+    if (in_dtype == HEPH_F32 && acc_dtype == HEPH_F64)
+        return launch_op<float, double>(dev, stream, op, base, l, count, out);
+    return fail(HEPH_INVALID_CONFIGURATION,
+                "full reduction output type must match the input type or widen it (i32->i64, "
+                "f32->f64)");
+}
+
+}  // namespace heph

@@ -1,0 +1,167 @@
+"""The reference's conformance clauses and CUDA contract cases, run through
+the seams on the GPU and compared exactly with the values the reference
+asserts (tests/golden/reference_fixtures.json, each case citing its source
+file:line in hephaestus)."""
+import numpy as np
+import pytest
+
+import hephaestus_b200.seams as S
+from hephaestus_b200 import (CudaAxisReductionOps, CudaFullReductionOps, CudaScanOps, DispatchFailed,
+                             Layout, MaxOp, MinOp, ProdOp, StridedView, SumOp)
+from hephaestus_b200.core import CumProdOp, CumSumOp
+from tests.golden_util import DT, cases_of_kind, load_cases
+
+pytestmark = pytest.mark.gpu
+
+OPS = {"sum": SumOp, "prod": ProdOp, "min": MinOp, "max": MaxOp}
+SCAN_OPS = {"sum": CumSumOp, "prod": CumProdOp}
+CASES = {c["id"]: c for c in load_cases()}
+
+
+def L(d):
+    return Layout.try_new(d["shape"], d["strides"], d["offset"])
+
+
+def upload_input(device, c):
+    a = np.array(c["input"], dtype=DT[c["dtype"]])
+    if a.size == 0:
+        return device.alloc_zeroed(a.dtype, 0), a
+    return device.upload(a), a
+
+
+@pytest.mark.parametrize("cid", cases_of_kind("reduce_full", "reduce_full_prepared"))
+def test_full_reduction_clause(device, cid):
+    c = CASES[cid]
+    buf, a = upload_input(device, c)
+    ops = CudaFullReductionOps()
+    ol = L(c["out_layout"]) if "out_layout" in c else Layout.c_contiguous([1])
+    init = np.array(c.get("out_init", [0] * ol.size()), dtype=a.dtype)
+    out = device.upload(init)
+    if "error" in c:
+        with pytest.raises(DispatchFailed) as e:
+            ops.reduce_full_into(OPS[c["op"]], device, StridedView(buf, L(c["layout"])), StridedView(out, ol))
+        assert e.value.message == c["error"], c["source"]
+        np.testing.assert_array_equal(device.download_owned(out), init)  # untouched
+        return
+    if c["kind"] == "reduce_full_prepared":
+        prep = ops.prepare_reduce_full(OPS[c["op"]], device, StridedView(buf, L(c["layout"])), StridedView(out, ol))
+        ops.dispatch_full(device, prep)
+        np.testing.assert_array_equal(device.download_owned(out), c["expected"])
+        ops.dispatch_full(device, prep)
+        np.testing.assert_array_equal(device.download_owned(out), c["expected"])
+        device.write_buffer(buf, np.array(c["rewrite"], dtype=a.dtype))
+        ops.dispatch_full(device, prep)
+        np.testing.assert_array_equal(device.download_owned(out), c["expected_after_rewrite"])
+        return
+    ops.reduce_full_into(OPS[c["op"]], device, StridedView(buf, L(c["layout"])), StridedView(out, ol))
+    np.testing.assert_array_equal(device.download_owned(out), np.array(c["expected"], dtype=a.dtype),
+                                  err_msg=c["source"])
+
+
+@pytest.mark.parametrize("cid", cases_of_kind("reduce_axis", "reduce_axis_prepared"))
+def test_axis_reduction_clause(device, cid):
+    c = CASES[cid]
+    buf, a = upload_input(device, c)
+    lay = L(c["layout"])
+    axis = c["axis"]
+    if "out_layout" in c:
+        ol = L(c["out_layout"])
+    else:
+        shape = list(lay.shape)
+        shape[axis] = 1
+        ol = Layout.c_contiguous(shape)
+    init = np.array(c.get("out_init", [0] * max(ol.size(), 1)), dtype=a.dtype)
+    out = device.upload(init)
+    ops = CudaAxisReductionOps()
+    op = c["op"]
+
+    def call():
+        if op == "mean":
+            ops.mean_axis_into(device, StridedView(buf, lay), axis, StridedView(out, ol))
+        elif op == "prod":
+            ops.prod_axis_into(device, StridedView(buf, lay), axis, StridedView(out, ol))
+        else:
+            ops.reduce_axis_into(OPS[op], device, StridedView(buf, lay), axis, StridedView(out, ol))
+
+    if "error" in c or "error_prefix" in c:
+        with pytest.raises(DispatchFailed) as e:
+            call()
+        if "error" in c:
+            assert e.value.message == c["error"], c["source"]
+        else:
+            assert e.value.message.startswith(c["error_prefix"]), c["source"]
+        np.testing.assert_array_equal(device.download_owned(out), init)
+        return
+    if c["kind"] == "reduce_axis_prepared":
+        prep = ops.prepare_reduce_axis_into(OPS[op], device, StridedView(buf, lay), axis, StridedView(out, ol))
+        for _ in range(2):
+            ops.dispatch_prepared(device, prep)
+            np.testing.assert_array_equal(device.download_owned(out), c["expected"])
+        device.write_buffer(buf, np.array(c["rewrite"], dtype=a.dtype))
+        ops.dispatch_prepared(device, prep)
+        np.testing.assert_array_equal(device.download_owned(out), c["expected_after_rewrite"])
+        return
+    call()
+    np.testing.assert_array_equal(device.download_owned(out), np.array(c["expected"], dtype=a.dtype),
+                                  err_msg=c["source"])
+
+
+@pytest.mark.parametrize("cid", cases_of_kind("scan", "scan_prepared"))
+def test_scan_clause(device, cid):
+    c = CASES[cid]
+    buf, a = upload_input(device, c)
+    lay = L(c["layout"])
+    ol = L(c["out_layout"]) if "out_layout" in c else lay
+    n = max(ol.size(), 1)
+    init = np.array(c.get("out_init", [0] * n), dtype=a.dtype)
+    out = device.upload(init) if init.size else device.alloc_zeroed(a.dtype, 0)
+    ops = CudaScanOps()
+    direction = 1 if c["reverse"] else 0
+    if "error" in c or "error_prefix" in c:
+        with pytest.raises(DispatchFailed) as e:
+            ops.scan_axis_into(SCAN_OPS[c["op"]], device, StridedView(buf, lay), c["axis"], direction,
+                               StridedView(out, ol))
+        if "error" in c:
+            assert e.value.message == c["error"], c["source"]
+        else:
+            assert e.value.message.startswith(c["error_prefix"]), c["source"]
+        np.testing.assert_array_equal(device.download_owned(out), init)
+        return
+    if c["kind"] == "scan_prepared":
+        prep = ops.prepare_scan_axis(SCAN_OPS[c["op"]], device, StridedView(buf, lay), c["axis"], direction,
+                                     StridedView(out, ol))
+        for _ in range(2):
+            ops.dispatch_scan(device, prep)
+            np.testing.assert_array_equal(device.download_owned(out), c["expected"])
+        device.write_buffer(buf, np.array(c["rewrite"], dtype=a.dtype))
+        ops.dispatch_scan(device, prep)
+        np.testing.assert_array_equal(device.download_owned(out), c["expected_after_rewrite"])
+        return
+    ops.scan_axis_into(SCAN_OPS[c["op"]], device, StridedView(buf, lay), c["axis"], direction,
+                       StridedView(out, ol))
+    got = device.download_owned(out)
+    np.testing.assert_array_equal(got[:len(c["expected"])], np.array(c["expected"], dtype=a.dtype),
+                                  err_msg=c["source"])
+
+
+def test_free_function_widths(device):
+    # contract.rs:670-690: width 128 works, 192 is rejected with the reference message.
+    host = np.arange(1027, dtype=np.uint32)
+    buf = device.upload(host)
+    out = S.reduction_with_width(SumOp, device, buf, 128)
+    assert device.download_owned(out)[0] == host.sum()
+    with pytest.raises(DispatchFailed) as e:
+        S.reduction_with_width(SumOp, device, buf, 192)
+    assert e.value.message == "reduction block width 192 must be a power of two"
+
+
+def test_allocating_scan_conveniences(device):
+    # contract.rs:1807-1911 through the allocating forms.
+    buf = device.upload(np.arange(1, 7, dtype=np.int32))
+    t = Layout.try_new([2, 3], [1, 2], 0)
+    got = device.download_owned(S.cumprod(device, StridedView(buf, t), 0))
+    np.testing.assert_array_equal(got, [1, 3, 5, 2, 12, 30])
+    got = device.download_owned(S.suffix_prod(device, StridedView(buf, t), 1))
+    np.testing.assert_array_equal(got, [15, 15, 5, 48, 24, 6])
+    empty = device.alloc_zeroed(np.int32, 0)
+    assert len(S.cumprod(device, StridedView(empty, Layout.c_contiguous([2, 0])), 1)) == 0

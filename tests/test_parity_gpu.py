@@ -1,0 +1,291 @@
+"""CUDA path vs the CPU oracle on seeded inputs: every element type and
+operator, sizes around every tile edge, unaligned offsets, strided and
+transposed views, reverse and exclusive scans, arg-reductions with ties.
+Integers and argmax indices bit-exact; f32 within 1e-5*sum|x|, f64 within
+1e-12*sum|x| (the tolerances the north star states)."""
+import numpy as np
+import pytest
+
+from hephaestus_b200 import (CudaAxisReductionOps, CudaFullReductionOps, CudaScanOps, Layout,
+                             MaxOp, MinOp, ProdOp, StridedView, SumOp)
+from hephaestus_b200.core import CumProdOp, CumSumOp
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = [np.float32, np.float64, np.uint32, np.int32, np.int64]
+OPS = {0: SumOp, 1: ProdOp, 2: MinOp, 3: MaxOp}
+SCAN_TILE = {4: 4096, 8: 2048}
+EDGE_SIZES = [0, 1, 2, 3, 31, 32, 33, 255, 256, 257, 1023, 1025, 2047, 2049, 4095, 4096, 4097,
+              8191, 8193, 65537, 1 << 20, (1 << 20) + 3]
+
+
+def rand(dt, n, rng, prod=False):
+    if np.dtype(dt).kind == "f":
+        if prod:
+            return rng.choice([0.5, 1.0, 2.0, -1.0], size=n).astype(dt)
+        return rng.uniform(-1, 1, size=n).astype(dt)
+    if prod:
+        return rng.choice([1, 3, 5, 7], size=n).astype(dt)  # odd: products never collapse to 0
+    lo = 0 if np.dtype(dt).kind == "u" else -1000
+    return rng.integers(lo, 1000, size=n).astype(dt)
+
+
+def tol(dt, x):
+    s = float(np.abs(x.astype(np.float64)).sum()) if x.size else 0.0
+    return {np.dtype(np.float32): 1e-5, np.dtype(np.float64): 1e-12}.get(np.dtype(dt), 0) * max(s, 1.0)
+
+
+def assert_close(got, want, dt, x):
+    if np.dtype(dt).kind == "f":
+        np.testing.assert_allclose(got.astype(np.float64), want.astype(np.float64), rtol=0,
+                                   atol=tol(dt, x))
+    else:
+        np.testing.assert_array_equal(got, want)
+
+
+# ----------------------------------------------------------- full reductions
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+@pytest.mark.parametrize("op", [0, 1, 2, 3])
+def test_full_reduction_edges(device, oracle, dt, op):
+    rng = np.random.default_rng(op * 10 + DTYPES.index(dt))
+    ops = CudaFullReductionOps()
+    for n in EDGE_SIZES:
+        if op == 1 and n > 4096:
+            continue
+        x = rand(dt, n, rng, prod=op == 1)
+        buf = device.upload(x) if n else device.alloc_zeroed(dt, 0)
+        out = device.alloc_zeroed(dt, 1)
+        ops.reduce_full_into(OPS[op], device, StridedView(buf, Layout.c_contiguous([n])),
+                             StridedView(out, Layout.c_contiguous([1])))
+        want = oracle.reduce_full(x, [n], op=op)
+        assert_close(device.download_owned(out), np.array([want], dtype=dt), dt, x)
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.uint32, np.int64])
+def test_full_reduction_unaligned_and_strided(device, oracle, dt):
+    rng = np.random.default_rng(3)
+    x = rand(dt, 100003, rng)
+    buf = device.upload(x)
+    ops = CudaFullReductionOps()
+    out = device.alloc_zeroed(dt, 4)
+    views = [
+        Layout.try_new([99990], [1], 5),          # unaligned dense
+        Layout.try_new([333, 300], [300, 1], 3),  # dense rank-2 with offset
+        Layout.try_new([300, 333], [1, 300], 1),  # transposed
+        Layout.try_new([50000], [2], 1),          # stride 2
+        Layout.try_new([1000], [-7], 7000),       # negative stride
+        Layout.try_new([10, 10, 10, 10], [10000, 1000, 10, 1], 17),
+    ]
+    for v in views:
+        ops.reduce_full_into(SumOp, device, StridedView(buf, v), StridedView(out, Layout.try_new([1], [1], 2)))
+        want = oracle.reduce_full(x, v.shape, v.strides, v.offset)
+        got = device.download_owned(out)[2:3]
+        assert_close(got, np.array([want], dtype=dt), dt, x)
+
+
+def test_widening_sums(device, oracle):
+    rng = np.random.default_rng(11)
+    x = rng.integers(-2**31, 2**31 - 1, size=300007, dtype=np.int64).astype(np.int32)
+    buf = device.upload(x)
+    out = device.alloc_zeroed(np.int64, 1)
+    CudaFullReductionOps().reduce_full_into(SumOp, device, StridedView(buf, Layout.c_contiguous([x.size])),
+                                            StridedView(out, Layout.c_contiguous([1])))
+    assert device.download_owned(out)[0] == int(x.astype(np.int64).sum())
+    assert oracle.reduce_full(x, [x.size], out_dtype=np.int64) == int(x.astype(np.int64).sum())
+    f = rng.uniform(-1, 1, size=300007).astype(np.float32)
+    fb = device.upload(f)
+    fo = device.alloc_zeroed(np.float64, 1)
+    CudaFullReductionOps().reduce_full_into(SumOp, device, StridedView(fb, Layout.c_contiguous([f.size])),
+                                            StridedView(fo, Layout.c_contiguous([1])))
+    assert abs(device.download_owned(fo)[0] - f.astype(np.float64).sum()) <= 1e-12 * np.abs(f).sum()
+
+
+# ------------------------------------------------------------ axis reductions
+
+AXIS_SHAPES = [(1, 1), (3, 4), (7, 33), (33, 7), (5, 4097), (4097, 5), (2, 70000), (70000, 2),
+               (129, 1024), (1024, 129), (1, 300000), (300000, 1)]
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+@pytest.mark.parametrize("op", [0, 2, 3, 4])
+def test_axis_reduction_shapes(device, oracle, dt, op):
+    rng = np.random.default_rng(op + 7 * DTYPES.index(dt))
+    ops = CudaAxisReductionOps()
+    for shape in AXIS_SHAPES:
+        x = rand(dt, shape[0] * shape[1], rng)
+        buf = device.upload(x)
+        for axis in (0, 1):
+            oshape = list(shape)
+            oshape[axis] = 1
+            out = device.alloc_zeroed(dt, oshape[0] * oshape[1])
+            ol = Layout.c_contiguous(oshape)
+            if op == 4:
+                ops.mean_axis_into(device, StridedView(buf, Layout.c_contiguous(shape)), axis, StridedView(out, ol))
+            else:
+                ops.reduce_axis_into(OPS[op], device, StridedView(buf, Layout.c_contiguous(shape)), axis,
+                                     StridedView(out, ol))
+            want = oracle.reduce_axis(x, shape, axis, op=op)
+            got = device.download_owned(out)
+            if op == 4 and np.dtype(dt).kind == "f":
+                np.testing.assert_allclose(got, want, rtol=1e-5 if dt == np.float32 else 1e-12, atol=1e-6)
+            else:
+                assert_close(got, want, dt, x)
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.int32])
+def test_axis_prod_and_strided_views(device, oracle, dt):
+    rng = np.random.default_rng(5)
+    x = rand(dt, 64 * 130 + 3, rng, prod=True)
+    buf = device.upload(x)
+    ops = CudaAxisReductionOps()
+    for lay in [Layout.try_new([64, 130], [130, 1], 3), Layout.try_new([130, 64], [1, 130], 0),
+                Layout.try_new([32, 130], [260, 1], 1), Layout.try_new([64, 65], [130, 2], 0)]:
+        for axis in (0, 1):
+            for op in (1, 0, 3):
+                oshape = list(lay.shape)
+                oshape[axis] = 1
+                out = device.alloc_zeroed(dt, oshape[0] * oshape[1])
+                ops.reduce_axis_into(OPS[op], device, StridedView(buf, lay), axis,
+                                     StridedView(out, Layout.c_contiguous(oshape)))
+                want = oracle.reduce_axis(x, lay.shape, axis, op=op, in_strides=lay.strides,
+                                          in_offset=lay.offset)
+                got = device.download_owned(out)
+                if op == 1 and np.dtype(dt).kind == "f":
+                    np.testing.assert_allclose(got, want, rtol=1e-5)
+                else:
+                    assert_close(got, want, dt, x)
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+@pytest.mark.parametrize("op", [3, 2])
+def test_arg_reduction_ties(device, oracle, dt, op):
+    rng = np.random.default_rng(17 + op)
+    ops = CudaAxisReductionOps()
+    for shape in [(3, 4), (33, 129), (5, 5000), (5000, 5), (1, 100000), (257, 4096)]:
+        # few distinct values: many exact ties
+        x = rng.integers(0, 7, size=shape[0] * shape[1]).astype(dt)
+        buf = device.upload(x)
+        for axis in (0, 1):
+            oshape = list(shape)
+            oshape[axis] = 1
+            n = oshape[0] * oshape[1]
+            vals, idx = device.alloc_zeroed(dt, n), device.alloc_zeroed(np.uint32, n)
+            ol = Layout.c_contiguous(oshape)
+            fn = ops.argmax_axis_into if op == 3 else ops.argmin_axis_into
+            fn(device, StridedView(buf, Layout.c_contiguous(shape)), axis, StridedView(vals, ol), StridedView(idx, ol))
+            wv, wi = oracle.arg_reduce_axis(x, shape, axis, op=op)
+            np.testing.assert_array_equal(device.download_owned(idx), wi)
+            np.testing.assert_array_equal(device.download_owned(vals), wv)
+
+
+def test_argmax_infinities(device, oracle):
+    x = np.full(64 * 40, -np.inf, dtype=np.float32)
+    x[5 * 40 + 7] = -1.0
+    buf = device.upload(x)
+    ops = CudaAxisReductionOps()
+    vals, idx = device.alloc_zeroed(np.float32, 64), device.alloc_zeroed(np.uint32, 64)
+    ol = Layout.c_contiguous([64, 1])
+    ops.argmax_axis_into(device, StridedView(buf, Layout.c_contiguous([64, 40])), 1, StridedView(vals, ol),
+                         StridedView(idx, ol))
+    wv, wi = oracle.arg_reduce_axis(x, [64, 40], 1)
+    np.testing.assert_array_equal(device.download_owned(idx), wi)
+    np.testing.assert_array_equal(device.download_owned(vals), wv)
+
+
+# --------------------------------------------------------------------- scans
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+@pytest.mark.parametrize("exclusive", [False, True])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_scan_1d_edges(device, oracle, dt, exclusive, reverse):
+    rng = np.random.default_rng(DTYPES.index(dt) * 4 + 2 * exclusive + reverse)
+    tile = SCAN_TILE[np.dtype(dt).itemsize]
+    sizes = sorted(set(EDGE_SIZES + [tile - 1, tile, tile + 1, 2 * tile - 1, 2 * tile + 1,
+                                     33 * tile + 5, 1000 * tile]))
+    ops = CudaScanOps()
+    for n in sizes:
+        x = rand(dt, n, rng)
+        buf = device.upload(x) if n else device.alloc_zeroed(dt, 0)
+        out = device.alloc_zeroed(dt, n)
+        ops.scan_axis_into(CumSumOp, device, StridedView(buf, Layout.c_contiguous([n])), 0, int(reverse),
+                           StridedView(out, Layout.c_contiguous([n])), exclusive=exclusive)
+        want = oracle.scan_axis(x, [n], 0, reverse=reverse, exclusive=exclusive)
+        got = device.download_owned(out)
+        if np.dtype(dt).kind == "f":
+            # float scans: |err| <= tol * sum|x| per element (ADR 0009 bound)
+            np.testing.assert_allclose(got.astype(np.float64), want.astype(np.float64), rtol=0,
+                                       atol=tol(dt, x))
+        else:
+            np.testing.assert_array_equal(got, want, err_msg=f"n={n}")
+
+
+@pytest.mark.parametrize("dt", [np.uint32, np.int64, np.float32])
+def test_scan_prod_and_unaligned(device, oracle, dt):
+    rng = np.random.default_rng(99)
+    x = rand(dt, 50001, rng, prod=True)
+    buf = device.upload(x)
+    out = device.alloc_zeroed(dt, 50001)
+    ops = CudaScanOps()
+    for off_in, off_out, n in [(0, 0, 50001), (1, 0, 50000), (3, 5, 49990), (2, 2, 40000)]:
+        for rev in (False, True):
+            ops.scan_axis_into(CumProdOp, device, StridedView(buf, Layout.try_new([n], [1], off_in)), 0, int(rev),
+                               StridedView(out, Layout.try_new([n], [1], off_out)))
+            want = oracle.scan_axis(x, [n], 0, op=1, reverse=rev, in_offset=off_in)
+            got = device.download_owned(out)[off_out:off_out + n]
+            if np.dtype(dt).kind == "f":
+                np.testing.assert_allclose(got, want[:n], rtol=1e-5)
+            else:
+                np.testing.assert_array_equal(got, want[:n])
+
+
+@pytest.mark.parametrize("dt", [np.uint32, np.int32, np.float64])
+def test_scan_2d_both_axes(device, oracle, dt):
+    rng = np.random.default_rng(5)
+    ops = CudaScanOps()
+    for shape in [(3, 4), (7, 5000), (5000, 7), (3, 20000), (64, 4097), (2, 513)]:
+        x = rand(dt, shape[0] * shape[1], rng)
+        buf = device.upload(x)
+        for axis in (0, 1):
+            for rev in (False, True):
+                for exc in (False, True):
+                    out = device.alloc_zeroed(dt, x.size)
+                    ops.scan_axis_into(CumSumOp, device, StridedView(buf, Layout.c_contiguous(shape)), axis, int(rev),
+                                       StridedView(out, Layout.c_contiguous(shape)), exclusive=exc)
+                    want = oracle.scan_axis(x, shape, axis, reverse=rev, exclusive=exc)
+                    got = device.download_owned(out)
+                    if np.dtype(dt).kind == "f":
+                        np.testing.assert_allclose(got, want, rtol=0, atol=1e-12 * max(1, np.abs(x).sum()))
+                    else:
+                        np.testing.assert_array_equal(got, want, err_msg=f"{shape} axis={axis} rev={rev} exc={exc}")
+
+
+def test_scan_transposed_output(device, oracle):
+    rng = np.random.default_rng(8)
+    x = rand(np.int32, 300 * 500, rng)
+    buf = device.upload(x)
+    out = device.alloc_zeroed(np.int32, x.size)
+    lin = Layout.c_contiguous([300, 500])
+    lout = Layout.try_new([300, 500], [1, 300], 0)
+    CudaScanOps().scan_axis_into(CumSumOp, device, StridedView(buf, lin), 1, 0, StridedView(out, lout))
+    want = oracle.scan_axis(x, [300, 500], 1, out_strides=[1, 300])
+    np.testing.assert_array_equal(device.download_owned(out), want)
+
+
+def test_repeated_scans_reuse_workspace(device, oracle):
+    """Many scans in a row on one stream: the epoch-tagged status and the
+    tile counter stay consistent (no clearing between calls)."""
+    rng = np.random.default_rng(1)
+    ops = CudaScanOps()
+    for k in range(40):
+        n = int(rng.integers(1, 300000))
+        dt = [np.uint32, np.int64][k % 2]
+        x = rand(dt, n, rng)
+        buf, out = device.upload(x), device.alloc_zeroed(dt, n)
+        ops.scan_axis_into(CumSumOp, device, StridedView(buf, Layout.c_contiguous([n])), 0, k % 3 == 0,
+                           StridedView(out, Layout.c_contiguous([n])), exclusive=k % 5 == 0)
+        want = oracle.scan_axis(x, [n], 0, reverse=k % 3 == 0, exclusive=k % 5 == 0)
+        np.testing.assert_array_equal(device.download_owned(out), want)
+    device.synchronize()  # no device-side error (look-back timeout) was raised
