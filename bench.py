@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--n", type=int, default=None,
+                    help="override the element count of configs 1, 2 and 5 (small profiling cases)")
     return ap.parse_args()
 
 
@@ -232,7 +234,10 @@ def run_reference(args, cfg):
 
 def main():
     args = parse()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.n is not None and "n" in cfg:
+        cfg["n"] = int(args.n)
+        cfg["workload"] += f" [reduced to {args.n} elements]"
     if args.impl == "reference":
         return run_reference(args, cfg)
 

@@ -33,7 +33,7 @@ class Layout_t(ctypes.Structure):
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
-        f"{LIB_PATH} is missing: build it with `python -m hephaestus_b200.build` "
+        f"{LIB_PATH} is missing: build it with `python hephaestus_b200/build.py` "
         "(nvcc, sm_100a); the reduce/scan path has no CPU fallback")
 
 lib = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)

@@ -3,7 +3,7 @@
 Every translation unit under ``csrc/`` is compiled to an object in
 ``_build/`` (in parallel, skipping up-to-date objects) and linked into
 ``hephaestus_b200/libheph_b200.so``.  Runs without a GPU (nvcc
-cross-compiles).  ``python -m hephaestus_b200.build [--verbose-ptxas]``.
+cross-compiles).  ``python hephaestus_b200/build.py [--verbose-ptxas]``.
 """
 from __future__ import annotations
 

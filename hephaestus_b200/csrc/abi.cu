@@ -114,6 +114,8 @@ static heph_status check_device_error(Device *dev) {
     unsigned int e = __atomic_exchange_n(dev->error_host, 0u, __ATOMIC_SEQ_CST);
     if (e & DEVERR_LOOKBACK_TIMEOUT)
         return fail(HEPH_DISPATCH_FAILED, "look-back timeout: a scan tile waited too long for its predecessor");
+    if (e & DEVERR_BULK_TIMEOUT)
+        return fail(HEPH_DISPATCH_FAILED, "bulk copy timeout: a scan part's input never arrived");
     if (e) return fail(HEPH_DISPATCH_FAILED, "device reported error code " + std::to_string(e));
     return HEPH_OK;
 }

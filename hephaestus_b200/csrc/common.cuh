@@ -143,8 +143,7 @@ struct Workspace {
     // Look-back status: flags (epoch-tagged) + aggregate / inclusive values.
     void *scan_status = nullptr;
     size_t scan_status_bytes = 0;
-    unsigned long long *tile_counter = nullptr;  // monotonically increasing
-    unsigned long long tiles_drawn = 0;           // host mirror of *tile_counter
+    unsigned long long *tile_counter = nullptr;  // reserved; zero at rest
     uint32_t epoch = 0;                           // tags this call's flags
     void *small = nullptr;                        // 256 bytes of per-call scalars
 };
@@ -179,7 +178,7 @@ heph_status workspace_for(Device *device, cudaStream_t stream, size_t partial_by
                           size_t scan_status_bytes, Workspace **out);
 
 // Device-side error codes written to Device::error_dev.
-enum DeviceError : unsigned int { DEVERR_LOOKBACK_TIMEOUT = 1u };
+enum DeviceError : unsigned int { DEVERR_LOOKBACK_TIMEOUT = 1u, DEVERR_BULK_TIMEOUT = 2u };
 
 }  // namespace heph
 

@@ -258,6 +258,7 @@ static heph_status launch_axis_typed(Device *dev, cudaStream_t stream, const T *
         }
         uint64_t seg = (p.len + splits - 1) / splits;
         seg = (seg + 32 * V - 1) / (32 * V) * (32 * V);  // vector-aligned segments
+        seg = std::max<uint64_t>(seg, 32 * V);             // an empty axis still gets one segment
         splits = std::max<uint64_t>(1, (p.len + seg - 1) / seg);
         a.splits = splits;
         a.seg = std::max<uint64_t>(seg, 1);

@@ -4,28 +4,32 @@
 // lane walks a private contiguous chunk, lane 0 folds the chunk totals
 // serially, and a second pass re-reads and rewrites the output
 // (core accelerator/scan.rs:94-147): a 1-D vector runs on a single SM and
-// moves 4N elements.  Here a line that is contiguous along the scan axis is
-// scanned by a single-pass decoupled look-back (Merrill & Garland, "Single-pass
-// Parallel Prefix Scan with Decoupled Look-back", NVIDIA TR 2016):
-//   * each CTA draws its tile id from an atomic counter (so every
-//     predecessor of a running tile has already started: forward progress
-//     does not depend on block scheduling order), loads its 16 KiB tile with
-//     128-bit streaming loads (4 vectors in flight per thread), scans it in
-//     registers (thread-local, then warp shuffles, then the 8 warp totals);
-//   * publishes its aggregate, looks back over its predecessors one warp
-//     window (32 tiles) at a time, publishes its inclusive prefix and writes
-//     the tile with 128-bit stores: 2N elements of traffic in one launch;
-//   * tile status words carry an epoch tag so the status array never needs
-//     clearing between calls; 4-byte element types pack (value, flag) in one
-//     64-bit word, 8-byte types use a flag word with release/acquire ordering;
-//   * every look-back wait is bounded: when it runs out the tile raises a
-//     device error bit (reported by synchronize as DispatchFailed), publishes
-//     a prefix anyway so its successors do not wait in turn, and finishes.
-// Reverse scans process the same physical tiles from the last one backwards
-// and mirror every intra-tile step.  Lines whose scan axis is not unit-stride
-// (column scans, transposed views) take a warp-per-line kernel that walks the
-// line in 32-element chunks with a warp scan and a running carry.
+// moves 4N elements.  Three kernels replace it, chosen by the shape of the
+// problem:
+//
+// * scan_chunked_kernel — one long contiguous line (the 1-D case).  A
+//   co-resident (cooperative) grid of G CTAs walks the line in chunks of G
+//   parts.  Each CTA keeps three of its parts in shared memory, filled by TMA
+//   bulk copies, so ~100 KiB of input per SM is always in flight.  Per chunk
+//   it reduces its next part, publishes the part's total, folds the totals of
+//   the parts before its own (read one chunk ahead), scans its part from
+//   shared memory and streams the results out.  HBM moves each element
+//   exactly twice and the only cross-CTA exchange is G totals per chunk.
+// * scan_lookback_kernel — contiguous lines too short (or too many) for the
+//   chunked kernel: single-pass decoupled look-back (Merrill & Garland,
+//   "Single-pass Parallel Prefix Scan with Decoupled Look-back", NVIDIA TR
+//   2016), one 32 KiB tile per CTA, tile id = blockIdx.x (blocks of a grid are
+//   dispatched in increasing order, so every predecessor of a running tile has
+//   been dispatched).  Measured on B200 the tile-prefix chain across the two
+//   dies bounds it near 3.5 TB/s for one long line, hence the chunked kernel.
+// * scan_strided_kernel — non-unit-stride scan axes (column scans, transposed
+//   views): one warp per line, 32 logical positions per step.
+//
+// All device-side waits are bounded: when a wait runs out the kernel raises a
+// device error bit (reported by synchronize as DispatchFailed), substitutes
+// the identity and finishes, so a fault never turns into a hang.
 #include <algorithm>
+#include <cstdlib>
 
 #include "device_utils.cuh"
 #include "kernels.h"
@@ -34,107 +38,80 @@ namespace heph {
 
 constexpr int kScanThreads = 256;
 constexpr int kScanWarps = kScanThreads / 32;
-constexpr uint32_t kLookbackPolls = 1u << 20;
+constexpr uint32_t kPolls = 1u << 20;        // bounded waits on other CTAs
+constexpr int kLookbackVectors = 8;          // look-back tile: 8 x 128-bit per thread (32 KiB)
+constexpr int kChunkVectors = 4;             // chunked kernel tile: 4 x 128-bit per thread (16 KiB)
+constexpr int kChunkMaxBuffers = 6;          // part buffers per CTA of the chunked scan
+constexpr int kChunkMaxPartsPerThread = 4;   // chunked grids have at most 4 x 256 CTAs
 
-template <typename T> struct ScanShape {
+// Scan status workspace, per entry (tile or part): a packed 64-bit word for
+// 4-byte types, then two 8-byte value arrays and a 32-bit flag array for
+// 8-byte types.  Section offsets are the entry capacity times 8, 16 and 24
+// bytes, so every 8-byte array stays 8-byte aligned for any capacity.
+constexpr size_t kStatusValsA = 8, kStatusValsB = 16, kStatusFlags = 24;
+constexpr size_t kStatusBytesPerEntry = 28;
+
+// Tuning knobs, read at each call (tests shrink the chunked kernel's parts).
+static int scan_knob(const char *name, int fallback) {
+    const char *e = getenv(name);
+    return e ? atoi(e) : fallback;
+}
+
+template <typename T, int JV> struct ScanShape {
     static constexpr int V = 16 / sizeof(T);  // elements per 128-bit vector
-    static constexpr int J = 4;               // vectors per thread
+    static constexpr int J = JV;              // vectors per thread
     static constexpr int WARP_ITEMS = 32 * V * J;
-    static constexpr int TILE = kScanThreads * V * J;  // 16 KiB
+    static constexpr int TILE = kScanThreads * V * J;
 };
 
 enum : uint32_t { kStateInvalid = 0, kStateAggregate = 1, kStatePrefix = 2 };
 
-template <typename T> struct ScanParams {
-    const T *in;
-    T *out;
-    uint64_t len;             // elements per line
-    uint64_t tiles_per_line;
-    int64_t in_line, out_line;  // element distance between line starts
-    unsigned long long *tile_counter;
-    unsigned long long tile_base;
+// ------------------------------------------------------------ status words
+
+struct StatusView {
     uint32_t epoch;
-    unsigned long long *packed;  // 4-byte T: (value << 32) | flag
-    uint32_t *flags;             // 8-byte T: flag words
-    T *aggs, *incls;             // 8-byte T: values
-    const T *carry;              // nullable seed of line 0
-    unsigned int *err;
-    int reverse, exclusive;
+    unsigned long long *packed;  // 4-byte T: (value << 32) | (epoch << 2) | state
+    uint32_t *flags;             // 8-byte T: (epoch << 2) | state
+    void *vals_a, *vals_b;       // 8-byte T: aggregate / inclusive values
 };
 
 template <typename T>
-__device__ __forceinline__ void publish(const ScanParams<T> &p, uint64_t tile, uint32_t state,
-                                        T value) {
-    const uint32_t f = (p.epoch << 2) | state;
+__device__ __forceinline__ void publish(const StatusView &s, uint64_t idx, uint32_t state, T value) {
+    const uint32_t f = (s.epoch << 2) | state;
     if constexpr (sizeof(T) == 4) {
-        const unsigned long long w =
-            ((unsigned long long)bitcast<uint32_t>(value) << 32) | f;
-        asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p.packed + tile), "l"(w)
-                     : "memory");
+        const unsigned long long w = ((unsigned long long)bitcast<uint32_t>(value) << 32) | f;
+        asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(s.packed + idx), "l"(w) : "memory");
     } else {
-        T *dst = (state == kStatePrefix ? p.incls : p.aggs) + tile;
-        asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(dst),
-                     "l"(bitcast<unsigned long long>(value))
+        T *dst = static_cast<T *>(state == kStatePrefix ? s.vals_b : s.vals_a) + idx;
+        asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(dst), "l"(bitcast<unsigned long long>(value))
                      : "memory");
-        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p.flags + tile), "r"(f)
-                     : "memory");
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(s.flags + idx), "r"(f) : "memory");
     }
 }
 
 template <typename T>
-__device__ __forceinline__ void read_status(const ScanParams<T> &p, uint64_t tile,
-                                            uint32_t &state, T &value) {
+__device__ __forceinline__ uint32_t read_status(const StatusView &s, uint64_t idx, T &value) {
     if constexpr (sizeof(T) == 4) {
         unsigned long long w;
-        asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p.packed + tile) : "memory");
-        const uint32_t f = (uint32_t)w;
-        state = ((f >> 2) == p.epoch) ? (f & 3u) : kStateInvalid;
+        asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(s.packed + idx) : "memory");
         value = bitcast<T>((uint32_t)(w >> 32));
+        const uint32_t f = (uint32_t)w;
+        return ((f >> 2) == s.epoch) ? (f & 3u) : kStateInvalid;
     } else {
         uint32_t f;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(f) : "l"(p.flags + tile) : "memory");
-        state = ((f >> 2) == p.epoch) ? (f & 3u) : kStateInvalid;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(f) : "l"(s.flags + idx) : "memory");
+        const uint32_t state = ((f >> 2) == s.epoch) ? (f & 3u) : kStateInvalid;
         if (state != kStateInvalid) {
-            const T *src = (state == kStatePrefix ? p.incls : p.aggs) + tile;
+            const T *src = static_cast<const T *>(state == kStatePrefix ? s.vals_b : s.vals_a) + idx;
             unsigned long long v;
             asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(src) : "memory");
             value = bitcast<T>(v);
         }
+        return state;
     }
 }
 
-// Exclusive prefix of `tile` within its line: fold of the predecessors back to
-// the nearest one that has published its inclusive prefix.  Runs on one warp.
-template <typename T, int OP>
-__device__ T lookback(const ScanParams<T> &p, uint64_t tile, uint64_t line_first, int lane,
-                      bool *timed_out) {
-    T excl = identity<T, OP>();
-    int64_t cur = (int64_t)tile - 1;
-    uint32_t polls = 0;
-    while (true) {
-        const int64_t idx = cur - lane;
-        const bool in_range = idx >= (int64_t)line_first;
-        uint32_t state = kStatePrefix;  // lanes before the line start act as an identity prefix
-        T val = identity<T, OP>();
-        if (in_range) read_status(p, (uint64_t)idx, state, val);
-        while (__any_sync(kFullMask, state == kStateInvalid)) {
-            if (++polls > kLookbackPolls) {
-                if (lane == 0) raise_device_error(p.err, DEVERR_LOOKBACK_TIMEOUT);
-                *timed_out = true;
-                return excl;
-            }
-            __nanosleep(64);
-            if (state == kStateInvalid) read_status(p, (uint64_t)idx, state, val);
-        }
-        const unsigned pm = __ballot_sync(kFullMask, state == kStatePrefix);
-        const int stop = pm ? __ffs(pm) - 1 : 31;
-        T v = lane <= stop ? val : identity<T, OP>();
-        v = warp_fold<T, OP>(v);
-        excl = combine<T, OP>(v, excl);
-        if (pm) return excl;
-        cur -= 32;
-    }
-}
+// ------------------------------------------------------------ tile scans
 
 // Inclusive warp scan in logical lane order (descending lanes when `rev`).
 template <typename T, int OP> __device__ __forceinline__ T warp_scan(T v, int lane, bool rev) {
@@ -147,54 +124,29 @@ template <typename T, int OP> __device__ __forceinline__ T warp_scan(T v, int la
     return v;
 }
 
-template <typename T, int OP, bool VEC>
-__global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const ScanParams<T> p) {
-    using S = ScanShape<T>;
-    constexpr int V = S::V, J = S::J, TILE = S::TILE;
-    __shared__ unsigned long long s_tile;
-    __shared__ T s_warp[kScanWarps];
-    __shared__ T s_prefix;
+// Physical position in the tile of thread (warp, lane)'s element (j, c) is
+// base + j*32*V + c with base = warp*WARP_ITEMS + lane*V: warp-striped
+// 128-bit vectors, so every load and store instruction of a warp covers 512
+// contiguous bytes.
+template <typename T, int JV> __device__ __forceinline__ int tile_base_pos(int warp, int lane) {
+    return warp * ScanShape<T, JV>::WARP_ITEMS + lane * ScanShape<T, JV>::V;
+}
 
+// Intra-tile part of a tile scan: in-vector inclusive scans (in place in x),
+// warp scans of the vector totals and the fold of the warp totals, all in
+// logical order (descending positions when `rev`).  Leaves the exclusive
+// prefix of every vector (pre), of the thread's warp (wpre) and the tile
+// aggregate (agg).  One __syncthreads; `s_warp` holds kScanWarps values.
+template <typename T, int JV> struct TileScan {
+    T pre[JV];
+    T wpre, agg;
+};
+
+template <typename T, int OP, int JV>
+__device__ __forceinline__ void tile_local_scan(T (&x)[JV][ScanShape<T, JV>::V], bool rev, T *s_warp,
+                                                TileScan<T, JV> &r) {
+    constexpr int V = ScanShape<T, JV>::V, J = JV;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (threadIdx.x == 0) s_tile = atomicAdd(p.tile_counter, 1ull) - p.tile_base;
-    __syncthreads();
-    const uint64_t tile = s_tile;
-    const uint64_t line = tile / p.tiles_per_line;
-    const uint64_t t_in_line = tile - line * p.tiles_per_line;
-    const bool rev = p.reverse != 0;
-    const uint64_t ptile = rev ? p.tiles_per_line - 1 - t_in_line : t_in_line;
-    const T *lin = p.in + (int64_t)line * p.in_line;
-    T *lout = p.out + (int64_t)line * p.out_line;
-    const uint64_t start = ptile * (uint64_t)TILE;
-    const uint64_t valid = min((uint64_t)TILE, p.len - start);
-    const bool full = VEC && valid == (uint64_t)TILE;
-    // Physical position in the tile of this thread's element (j, c):
-    // base + j*32*V + c — warp-striped 128-bit vectors, coalesced per j.
-    const int base = warp * S::WARP_ITEMS + lane * V;
-
-    T x[J][V];
-    if (full) {
-        uint4 raw[J];
-#pragma unroll
-        for (int j = 0; j < J; ++j)
-            raw[j] = ld_stream(reinterpret_cast<const uint4 *>(lin + start + base + j * 32 * V));
-#pragma unroll
-        for (int j = 0; j < J; ++j) {
-            Vec16<T> e = as_elems<T>(raw[j]);
-#pragma unroll
-            for (int c = 0; c < V; ++c) x[j][c] = e.e[c];
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < J; ++j)
-#pragma unroll
-            for (int c = 0; c < V; ++c) {
-                const uint64_t pos = (uint64_t)(base + j * 32 * V + c);
-                x[j][c] = pos < valid ? lin[start + pos] : identity<T, OP>();
-            }
-    }
-
-    // Inclusive scan inside each vector, in logical order.
     T tt[J];
 #pragma unroll
     for (int j = 0; j < J; ++j) {
@@ -208,9 +160,6 @@ __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const ScanP
             tt[j] = x[j][0];
         }
     }
-
-    // Warp scans of the vector totals, chunk by chunk in logical order.
-    T pre[J];
     T running = identity<T, OP>();
     const bool first_lane = rev ? (lane == 31) : (lane == 0);
 #pragma unroll
@@ -220,46 +169,34 @@ __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const ScanP
         T exc = rev ? shfl_down(inc, 1) : shfl_up(inc, 1);
         if (first_lane) exc = identity<T, OP>();
         const T tot = shfl_idx(inc, rev ? 0 : 31);
-        pre[jp] = combine<T, OP>(running, exc);
+        r.pre[jp] = combine<T, OP>(running, exc);
         running = combine<T, OP>(running, tot);
     }
-
-    // Block: fold the warp totals in logical warp order.
     if (lane == 0) s_warp[warp] = running;
     __syncthreads();
-    T wpre = identity<T, OP>(), agg = identity<T, OP>();
+    r.wpre = identity<T, OP>();
+    r.agg = identity<T, OP>();
 #pragma unroll
     for (int wl = 0; wl < kScanWarps; ++wl) {
         const int wp = rev ? kScanWarps - 1 - wl : wl;
-        if (wp == warp) wpre = agg;
-        agg = combine<T, OP>(agg, s_warp[wp]);
+        if (wp == warp) r.wpre = r.agg;
+        r.agg = combine<T, OP>(r.agg, s_warp[wp]);
     }
+}
 
-    // Tile prefix: seed for the first tile of a line, look-back otherwise.
-    if (warp == 0) {
-        T tp;
-        if (t_in_line == 0) {
-            tp = (p.carry != nullptr && line == 0) ? *p.carry : identity<T, OP>();
-            if (lane == 0) publish(p, tile, kStatePrefix, combine<T, OP>(tp, agg));
-        } else {
-            if (lane == 0) publish(p, tile, kStateAggregate, agg);
-            bool timed_out = false;
-            tp = lookback<T, OP>(p, tile, tile - t_in_line, lane, &timed_out);
-            if (lane == 0) publish(p, tile, kStatePrefix, combine<T, OP>(tp, agg));
-        }
-        if (lane == 0) s_prefix = tp;
-    }
-    __syncthreads();
-    const T thread_base = combine<T, OP>(s_prefix, wpre);
-
-    // Outputs.
-    T y[J][V];
+// Final values of the tile given the exclusive prefix of the whole tile.
+template <typename T, int OP, int JV>
+__device__ __forceinline__ void tile_outputs(const T (&x)[JV][ScanShape<T, JV>::V], const TileScan<T, JV> &r,
+                                             T tile_prefix, bool rev, bool exclusive,
+                                             T (&y)[JV][ScanShape<T, JV>::V]) {
+    constexpr int V = ScanShape<T, JV>::V;
+    const T thread_base = combine<T, OP>(tile_prefix, r.wpre);
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-        const T tpj = combine<T, OP>(thread_base, pre[j]);
+    for (int j = 0; j < JV; ++j) {
+        const T tpj = combine<T, OP>(thread_base, r.pre[j]);
 #pragma unroll
         for (int c = 0; c < V; ++c) {
-            if (p.exclusive) {
+            if (exclusive) {
                 const bool first = rev ? (c == V - 1) : (c == 0);
                 const T prev = rev ? x[j][(c + 1) % V] : x[j][(c + V - 1) % V];
                 y[j][c] = first ? tpj : combine<T, OP>(tpj, prev);
@@ -268,22 +205,346 @@ __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const ScanP
             }
         }
     }
+}
+
+// Loads a full tile with 128-bit loads from global or shared memory.
+template <typename T, int JV>
+__device__ __forceinline__ void load_tile_vec(const T *src, int base, T (&x)[JV][ScanShape<T, JV>::V],
+                                              bool streaming) {
+    constexpr int V = ScanShape<T, JV>::V;
+    uint4 raw[JV];
+#pragma unroll
+    for (int j = 0; j < JV; ++j) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(src + base + j * 32 * V);
+        raw[j] = streaming ? ld_stream(p) : *p;
+    }
+#pragma unroll
+    for (int j = 0; j < JV; ++j) {
+        Vec16<T> e = as_elems<T>(raw[j]);
+#pragma unroll
+        for (int c = 0; c < V; ++c) x[j][c] = e.e[c];
+    }
+}
+
+// Guarded element loads of a partial (or unaligned) tile; identity padding.
+template <typename T, int OP, int JV>
+__device__ __forceinline__ void load_tile_scalar(const T *src, uint64_t valid, int base,
+                                                 T (&x)[JV][ScanShape<T, JV>::V]) {
+    constexpr int V = ScanShape<T, JV>::V;
+#pragma unroll
+    for (int j = 0; j < JV; ++j)
+#pragma unroll
+        for (int c = 0; c < V; ++c) {
+            const uint64_t pos = (uint64_t)(base + j * 32 * V + c);
+            x[j][c] = pos < valid ? src[pos] : identity<T, OP>();
+        }
+}
+
+template <typename T, int JV>
+__device__ __forceinline__ void store_tile(T *dst, uint64_t valid, bool full, int base,
+                                           const T (&y)[JV][ScanShape<T, JV>::V]) {
+    constexpr int V = ScanShape<T, JV>::V;
     if (full) {
 #pragma unroll
-        for (int j = 0; j < J; ++j) {
+        for (int j = 0; j < JV; ++j) {
             Vec16<T> e;
 #pragma unroll
             for (int c = 0; c < V; ++c) e.e[c] = y[j][c];
-            *reinterpret_cast<uint4 *>(lout + start + base + j * 32 * V) = as_uint4(e);
+            st_stream(reinterpret_cast<uint4 *>(dst + base + j * 32 * V), as_uint4(e));
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < J; ++j)
+        for (int j = 0; j < JV; ++j)
 #pragma unroll
             for (int c = 0; c < V; ++c) {
                 const uint64_t pos = (uint64_t)(base + j * 32 * V + c);
-                if (pos < valid) lout[start + pos] = y[j][c];
+                if (pos < valid) dst[pos] = y[j][c];
             }
+    }
+}
+
+// --------------------------------------------------- decoupled look-back
+
+template <typename T> struct LookbackParams {
+    const T *in;
+    T *out;
+    uint64_t len;               // elements per line
+    uint64_t tiles_per_line;
+    int64_t in_line, out_line;  // element distance between line starts
+    StatusView status;
+    const T *carry;             // nullable seed of line 0
+    unsigned int *err;
+    int reverse, exclusive;
+};
+
+// Exclusive prefix of `tile` within its line: fold of the predecessors back
+// to the nearest one that has published its inclusive prefix, 32 predecessors
+// per round trip.  Runs on one warp.
+template <typename T, int OP>
+__device__ T lookback(const LookbackParams<T> &p, uint64_t tile, uint64_t line_first, int lane) {
+    T excl = identity<T, OP>();
+    int64_t cur = (int64_t)tile - 1;
+    uint32_t polls = 0;
+    while (true) {
+        const int64_t idx = cur - lane;
+        const bool in_range = idx >= (int64_t)line_first;
+        uint32_t state = kStatePrefix;  // positions before the line start act as an identity prefix
+        T val = identity<T, OP>();
+        if (in_range) state = read_status(p.status, (uint64_t)idx, val);
+        while (__any_sync(kFullMask, state == kStateInvalid)) {
+            if (++polls > kPolls) {
+                if (lane == 0) raise_device_error(p.err, DEVERR_LOOKBACK_TIMEOUT);
+                return excl;
+            }
+            __nanosleep(32);
+            if (state == kStateInvalid) state = read_status(p.status, (uint64_t)idx, val);
+        }
+        const unsigned pm = __ballot_sync(kFullMask, state == kStatePrefix);
+        const int stop = pm ? __ffs(pm) - 1 : 31;
+        T v = lane <= stop ? val : identity<T, OP>();
+        v = warp_fold<T, OP>(v);
+        excl = combine<T, OP>(v, excl);
+        if (pm) return excl;
+        cur -= 32;
+    }
+}
+
+// One tile per CTA; tiles of a line are numbered in scan order.
+template <typename T, int OP, bool VEC, int JV>
+__global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const LookbackParams<T> p) {
+    using S = ScanShape<T, JV>;
+    constexpr int V = S::V, TILE = S::TILE;
+    __shared__ T s_warp[kScanWarps];
+    __shared__ T s_prefix;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool rev = p.reverse != 0;
+    const uint64_t tile = blockIdx.x;
+    const uint64_t line = tile / p.tiles_per_line;
+    const uint64_t t_in_line = tile - line * p.tiles_per_line;
+    const uint64_t ptile = rev ? p.tiles_per_line - 1 - t_in_line : t_in_line;
+    const T *lin = p.in + (int64_t)line * p.in_line;
+    T *lout = p.out + (int64_t)line * p.out_line;
+    const uint64_t start = ptile * (uint64_t)TILE;
+    const uint64_t valid = min((uint64_t)TILE, p.len - start);
+    const bool full = VEC && valid == (uint64_t)TILE;
+    const int base = tile_base_pos<T, JV>(warp, lane);
+
+    T x[JV][V];
+    if (full) load_tile_vec<T, JV>(lin + start, base, x, true);
+    else load_tile_scalar<T, OP, JV>(lin + start, valid, base, x);
+    TileScan<T, JV> r;
+    tile_local_scan<T, OP, JV>(x, rev, s_warp, r);
+
+    if (warp == 0) {
+        T tp;
+        if (t_in_line == 0) {
+            tp = (p.carry != nullptr && line == 0) ? *p.carry : identity<T, OP>();
+            if (lane == 0) publish(p.status, tile, kStatePrefix, combine<T, OP>(tp, r.agg));
+        } else {
+            if (lane == 0) publish(p.status, tile, kStateAggregate, r.agg);
+            tp = lookback<T, OP>(p, tile, tile - t_in_line, lane);
+            if (lane == 0) publish(p.status, tile, kStatePrefix, combine<T, OP>(tp, r.agg));
+        }
+        if (lane == 0) s_prefix = tp;
+    }
+    __syncthreads();
+    T y[JV][V];
+    tile_outputs<T, OP, JV>(x, r, s_prefix, rev, p.exclusive != 0, y);
+    store_tile<T, JV>(lout + start, valid, full, base, y);
+}
+
+// --------------------------------- chunked reduce-then-scan, parts in smem
+
+template <typename T> struct ChunkParams {
+    const T *in;
+    T *out;
+    uint64_t len;
+    uint64_t part;     // elements per CTA per chunk (a multiple of the tile)
+    uint64_t chunk;    // part * gridDim.x
+    uint64_t nchunks;
+    StatusView status;
+    const T *carry;
+    unsigned int *err;
+    int reverse, exclusive;
+    int buffers;       // shared-memory part buffers per CTA (2..kChunkMaxBuffers)
+};
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// Thread 0: expect `bytes` on `bar` and start a bulk global->shared copy
+// (no multicast; the source is this GPU's own memory).
+__device__ __forceinline__ void bulk_load(void *dst_smem, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst_smem)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
+// Waits for phase `parity` of `bar`.  Bounded: after the poll budget the
+// device error bit is raised and the wait gives up.
+__device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, unsigned int *err) {
+    for (uint32_t polls = 0; polls < (1u << 26); ++polls) {
+        uint32_t done;
+        asm volatile("{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n selp.u32 %0, 1, 0, P;\n}"
+                     : "=r"(done)
+                     : "r"(smem_addr(bar)), "r"(parity)
+                     : "memory");
+        if (done) return;
+    }
+    if (threadIdx.x == 0) raise_device_error(err, DEVERR_BULK_TIMEOUT);
+}
+
+template <typename T, int OP, int JV>
+__global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkParams<T> p) {
+    using S = ScanShape<T, JV>;
+    constexpr int V = S::V, TILE = S::TILE;
+    extern __shared__ __align__(128) unsigned char dyn_smem[];
+    T *buf = reinterpret_cast<T *>(dyn_smem);  // buffers x part elements
+    __shared__ uint64_t bar[kChunkMaxBuffers];
+    __shared__ T s_warp[2][kScanWarps];
+    __shared__ T s_red[kScanWarps];
+    __shared__ T s_red2[kScanWarps];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int G = gridDim.x, b = blockIdx.x;
+    const int NB = p.buffers;
+    const bool rev = p.reverse != 0, excl = p.exclusive != 0;
+    const int base = tile_base_pos<T, JV>(warp, lane);
+    uint32_t phases = 0;
+
+    auto part_range = [&](uint64_t c, uint64_t &lo, uint64_t &hi) {
+        const uint64_t pc = rev ? p.nchunks - 1 - c : c;
+        lo = min(p.len, pc * p.chunk + (uint64_t)b * p.part);
+        hi = min(p.len, lo + p.part);
+    };
+    // Thread 0: start the bulk copy of this CTA's part of logical chunk c
+    // (full parts only; a ragged final part is read from global memory).
+    auto stage_in = [&](uint64_t c) {
+        uint64_t lo, hi;
+        part_range(c, lo, hi);
+        if (hi - lo == p.part)
+            bulk_load(buf + (c % NB) * p.part, p.in + lo, (uint32_t)(p.part * sizeof(T)), &bar[c % NB]);
+    };
+
+    // Step 1: total of this CTA's part of logical chunk c.
+    auto reduce_part = [&](uint64_t c) {
+        uint64_t lo, hi;
+        part_range(c, lo, hi);
+        const uint64_t n = hi - lo;
+        T acc = identity<T, OP>();
+        if (n == p.part) {
+            const int k = (int)(c % NB);
+            mbar_wait(&bar[k], (phases >> k) & 1u, p.err);
+            phases ^= 1u << k;
+            const uint4 *v = reinterpret_cast<const uint4 *>(buf + k * p.part);
+            for (uint64_t q = threadIdx.x; q < n / V; q += kScanThreads) {
+                Vec16<T> e = as_elems<T>(v[q]);
+#pragma unroll
+                for (int t = 0; t < V; ++t) acc = combine<T, OP>(acc, e.e[t]);
+            }
+        } else {
+            for (uint64_t e = lo + threadIdx.x; e < hi; e += kScanThreads) acc = combine<T, OP>(acc, p.in[e]);
+        }
+        acc = block_fold<T, OP, kScanThreads>(acc, s_red);
+        if (threadIdx.x == 0) publish(p.status, c * G + b, kStatePrefix, acc);
+    };
+
+    // Status words of chunk c's part totals (4-byte types), loaded one chunk
+    // ahead without waiting; validated when the totals are needed.
+    unsigned long long pf[kChunkMaxPartsPerThread];
+    auto prefetch = [&](uint64_t c) {
+        if constexpr (sizeof(T) == 4) {
+#pragma unroll
+            for (int i = 0; i < kChunkMaxPartsPerThread; ++i) {
+                const int q = threadIdx.x + i * kScanThreads;
+                if (q < G)
+                    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];"
+                                 : "=l"(pf[i])
+                                 : "l"(p.status.packed + c * G + q)
+                                 : "memory");
+            }
+        }
+    };
+
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < NB; ++k) mbar_init(&bar[k], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int k = 0; k < NB && (uint64_t)k < p.nchunks; ++k) stage_in(k);
+    }
+    __syncthreads();
+
+    T carry = p.carry ? *p.carry : identity<T, OP>();
+    if (p.nchunks > 0) {
+        reduce_part(0);
+        prefetch(0);
+    }
+    int parity = 0;
+    for (uint64_t c = 0; c < p.nchunks; ++c) {
+        if (c + 1 < p.nchunks) reduce_part(c + 1);
+
+        // Step 2: the part totals of chunk c.
+        T before = identity<T, OP>(), total = identity<T, OP>();
+#pragma unroll
+        for (int i = 0; i < kChunkMaxPartsPerThread; ++i) {
+            const int q = threadIdx.x + i * kScanThreads;
+            if (q >= G) break;
+            T v = identity<T, OP>();
+            bool ok;
+            if constexpr (sizeof(T) == 4) {
+                v = bitcast<T>((uint32_t)(pf[i] >> 32));
+                ok = ((uint32_t)pf[i] >> 2) == p.status.epoch;
+            } else {
+                ok = read_status(p.status, c * G + q, v) != kStateInvalid;
+            }
+            uint32_t polls = 0;
+            while (!ok) {
+                if (++polls > kPolls) {
+                    raise_device_error(p.err, DEVERR_LOOKBACK_TIMEOUT);
+                    v = identity<T, OP>();
+                    break;
+                }
+                __nanosleep(32);
+                ok = read_status(p.status, c * G + q, v) != kStateInvalid;
+            }
+            total = combine<T, OP>(total, v);
+            if (rev ? (q > b) : (q < b)) before = combine<T, OP>(before, v);
+        }
+        before = block_fold<T, OP, kScanThreads>(before, s_red);
+        total = block_fold<T, OP, kScanThreads>(total, s_red2);
+        if (c + 1 < p.nchunks) prefetch(c + 1);
+        T run = combine<T, OP>(carry, before);
+        carry = combine<T, OP>(carry, total);
+
+        // Step 3: scan the part in tiles, in logical order.
+        uint64_t lo, hi;
+        part_range(c, lo, hi);
+        const bool staged = hi - lo == p.part;  // landed: step 1 waited for it
+        const T *src = staged ? buf + (c % NB) * p.part : p.in + lo;
+        const uint64_t ntiles = (hi - lo + TILE - 1) / TILE;
+        for (uint64_t tl = 0; tl < ntiles; ++tl) {
+            const uint64_t tp = rev ? ntiles - 1 - tl : tl;
+            const uint64_t start = tp * TILE;  // relative to lo
+            const uint64_t valid = min((uint64_t)TILE, hi - lo - start);
+            const bool full = valid == (uint64_t)TILE;
+            T x[JV][V];
+            if (full) load_tile_vec<T, JV>(src + start, base, x, false);
+            else load_tile_scalar<T, OP, JV>(src + start, valid, base, x);
+            TileScan<T, JV> r;
+            tile_local_scan<T, OP, JV>(x, rev, s_warp[parity], r);
+            parity ^= 1;
+            T y[JV][V];
+            tile_outputs<T, OP, JV>(x, r, run, rev, excl, y);
+            run = combine<T, OP>(run, r.agg);
+            store_tile<T, JV>(p.out + lo + start, valid, full, base, y);
+        }
+        // Every thread is done with buffer c%NB: refill it with chunk c+NB.
+        __syncthreads();
+        if (threadIdx.x == 0 && c + NB < p.nchunks) stage_in(c + NB);
     }
 }
 
@@ -324,13 +585,80 @@ __global__ void __launch_bounds__(256) scan_strided_kernel(const StridedScanPara
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Status view over the workspace for `entries` entries; bumps the epoch
+// (clearing the status before the 30-bit tag wraps).  Caller holds dev->mu.
+static heph_status status_for(Device *dev, cudaStream_t stream, uint64_t entries, StatusView *sv) {
+    Workspace *ws = nullptr;
+    heph_status st = workspace_for(dev, stream, 0, (size_t)entries * kStatusBytesPerEntry, &ws);
+    if (st != HEPH_OK) return st;
+    if (ws->epoch >= (1u << 30) - 1) {
+        HEPH_CUDA_TRY(cudaMemsetAsync(ws->scan_status, 0, ws->scan_status_bytes, stream), HEPH_DISPATCH_FAILED,
+                      "scan status reset");
+        ws->epoch = 0;
+    }
+    ws->epoch += 1;
+    char *base = static_cast<char *>(ws->scan_status);
+    const size_t cap = ws->scan_status_bytes / kStatusBytesPerEntry;
+    sv->epoch = ws->epoch;
+    sv->packed = reinterpret_cast<unsigned long long *>(base);
+    sv->vals_a = base + cap * kStatusValsA;
+    sv->vals_b = base + cap * kStatusValsB;
+    sv->flags = reinterpret_cast<uint32_t *>(base + cap * kStatusFlags);
+    return HEPH_OK;
+}
+
+// The chunked kernel for one long aligned line.  Returns false (nothing
+// launched) when the line is too short to give every CTA four parts.
 template <typename T, int OP>
-static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *in, T *out,
-                                     const AxisProblem &pr, bool reverse, bool exclusive,
-                                     const T *carry) {
-    using S = ScanShape<T>;
+static bool launch_chunked(Device *dev, cudaStream_t stream, const T *in, T *out, uint64_t len, bool reverse,
+                           bool exclusive, const T *carry, heph_status *st) {
+    using S = ScanShape<T, kChunkVectors>;
+    const int nb = std::min(kChunkMaxBuffers, std::max(2, scan_knob("HEPH_SCAN_BUFS", 3)));
+    const uint64_t part_bytes = (uint64_t)std::max(16, scan_knob("HEPH_SCAN_PART_KB", 32)) << 10;
+    const uint64_t part = std::max<uint64_t>(1, part_bytes / sizeof(T) / S::TILE) * S::TILE;
+    const size_t smem = (size_t)nb * part * sizeof(T);
+    if (smem > (200u << 10)) return false;
+    auto kernel = scan_chunked_kernel<T, OP, kChunkVectors>;
+    int nb_sm = 0;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb_sm, kernel, kScanThreads, smem) != cudaSuccess ||
+        nb_sm < 1) {
+        cudaGetLastError();
+        return false;
+    }
+    const int per_sm = std::min(nb_sm, std::max(1, scan_knob("HEPH_SCAN_CHUNK_CTAS", 2)));
+    const uint64_t G =
+        std::min<uint64_t>((uint64_t)dev->sm_count * per_sm, (uint64_t)kChunkMaxPartsPerThread * kScanThreads);
+    if (len < 4 * part * G) return false;
+    ChunkParams<T> cp{};
+    cp.in = in;
+    cp.out = out;
+    cp.len = len;
+    cp.part = part;
+    cp.chunk = part * G;
+    cp.nchunks = (len + cp.chunk - 1) / cp.chunk;
+    cp.carry = carry;
+    cp.err = dev->error_dev;
+    cp.reverse = reverse;
+    cp.exclusive = exclusive;
+    cp.buffers = nb;
+    *st = status_for(dev, stream, cp.nchunks * G, &cp.status);
+    if (*st != HEPH_OK) return true;
+    void *args[] = {&cp};
+    // Cooperative launch: every CTA is co-resident, so CTAs may wait on each
+    // other's part totals.
+    cudaError_t e = cudaLaunchCooperativeKernel((const void *)kernel, dim3((unsigned)G), dim3(kScanThreads), args,
+                                                smem, stream);
+    *st = e == cudaSuccess ? HEPH_OK : cuda_fail(HEPH_DISPATCH_FAILED, e, "chunked scan launch");
+    return true;
+}
+
+template <typename T, int OP>
+static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *in, T *out, const AxisProblem &pr,
+                                     bool reverse, bool exclusive, const T *carry) {
+    using S = ScanShape<T, kLookbackVectors>;
     const bool contiguous = pr.in_r == 1 && pr.out_r == 1;
-    if (!contiguous || pr.len < (uint64_t)S::TILE / 2) {
+    if (!contiguous || pr.len < (uint64_t)S::TILE / 4) {
         StridedScanParams<T> sp{in, out, pr.outer, pr.len, pr.in_base, pr.in_o, pr.in_r,
                                 pr.out_base, pr.out_o, pr.out_r, carry, reverse, exclusive};
         const uint64_t blocks = (pr.outer * 32 + 255) / 256;
@@ -339,59 +667,42 @@ static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *
         HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "scan launch");
         return HEPH_OK;
     }
-    const uint64_t tiles_per_line = (pr.len + S::TILE - 1) / S::TILE;
-    const uint64_t tiles = tiles_per_line * pr.outer;
-    if (tiles > 0x7fffffffull) return fail(HEPH_DISPATCH_FAILED, "scan grid too large");
     const bool vec = aligned16(in + pr.in_base) && aligned16(out + pr.out_base) &&
                      (pr.outer == 1 || (((uint64_t)pr.in_o * sizeof(T)) % 16 == 0 &&
                                         ((uint64_t)pr.out_o * sizeof(T)) % 16 == 0));
-
     std::lock_guard<std::mutex> lock(dev->mu);
-    Workspace *ws = nullptr;
-    // Status layout: [packed u64 x tiles][flags u32 x tiles][aggs 8B x tiles][incls 8B x tiles]
-    const size_t status_bytes = (size_t)tiles * (8 + 4 + 8 + 8);
-    heph_status st = workspace_for(dev, stream, 0, status_bytes, &ws);
-    if (st != HEPH_OK) return st;
-    // Epoch tag: flags of earlier calls never match; restart (after clearing)
-    // before the 30-bit tag wraps.
-    if (ws->epoch >= (1u << 30) - 1) {
-        HEPH_CUDA_TRY(cudaMemsetAsync(ws->scan_status, 0, ws->scan_status_bytes, stream),
-                      HEPH_DISPATCH_FAILED, "scan status reset");
-        ws->epoch = 0;
+    if (vec && pr.outer == 1 && !scan_knob("HEPH_SCAN_NO_CHUNKED", 0)) {
+        heph_status st = HEPH_OK;
+        if (launch_chunked<T, OP>(dev, stream, in + pr.in_base, out + pr.out_base, pr.len, reverse, exclusive,
+                                  carry, &st))
+            return st;
     }
-    ws->epoch += 1;
-    char *sbase = static_cast<char *>(ws->scan_status);
-    const size_t cap = ws->scan_status_bytes / (8 + 4 + 8 + 8);
-    ScanParams<T> p{};
+    const uint64_t tiles_per_line = (pr.len + S::TILE - 1) / S::TILE;
+    const uint64_t tiles = tiles_per_line * pr.outer;
+    if (tiles > 0x7fffffffull) return fail(HEPH_DISPATCH_FAILED, "scan grid too large");
+    LookbackParams<T> p{};
+    heph_status st = status_for(dev, stream, tiles, &p.status);
+    if (st != HEPH_OK) return st;
     p.in = in + pr.in_base;
     p.out = out + pr.out_base;
     p.len = pr.len;
     p.tiles_per_line = tiles_per_line;
     p.in_line = pr.in_o;
     p.out_line = pr.out_o;
-    p.tile_counter = ws->tile_counter;
-    p.tile_base = ws->tiles_drawn;
-    p.epoch = ws->epoch;
-    p.packed = reinterpret_cast<unsigned long long *>(sbase);
-    p.flags = reinterpret_cast<uint32_t *>(sbase + cap * 8);
-    p.aggs = reinterpret_cast<T *>(sbase + cap * 12);
-    p.incls = reinterpret_cast<T *>(sbase + cap * 20);
     p.carry = carry;
     p.err = dev->error_dev;
     p.reverse = reverse;
     p.exclusive = exclusive;
     if (vec)
-        scan_lookback_kernel<T, OP, true><<<(unsigned)tiles, kScanThreads, 0, stream>>>(p);
+        scan_lookback_kernel<T, OP, true, kLookbackVectors><<<(unsigned)tiles, kScanThreads, 0, stream>>>(p);
     else
-        scan_lookback_kernel<T, OP, false><<<(unsigned)tiles, kScanThreads, 0, stream>>>(p);
+        scan_lookback_kernel<T, OP, false, kLookbackVectors><<<(unsigned)tiles, kScanThreads, 0, stream>>>(p);
     HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "scan launch");
-    ws->tiles_drawn += tiles;
     return HEPH_OK;
 }
 
-heph_status launch_scan(Device *dev, cudaStream_t stream, int op, heph_dtype dtype,
-                        const void *in, void *out, const AxisProblem &p, bool reverse,
-                        bool exclusive, const void *carry) {
+heph_status launch_scan(Device *dev, cudaStream_t stream, int op, heph_dtype dtype, const void *in, void *out,
+                        const AxisProblem &p, bool reverse, bool exclusive, const void *carry) {
     return dispatch_dtype(dtype, [&]<typename T>() -> heph_status {
         const T *ti = static_cast<const T *>(in);
         T *to = static_cast<T *>(out);

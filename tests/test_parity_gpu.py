@@ -21,8 +21,8 @@ EDGE_SIZES = [0, 1, 2, 3, 31, 32, 33, 255, 256, 257, 1023, 1025, 2047, 2049, 409
 
 def rand(dt, n, rng, prod=False):
     if np.dtype(dt).kind == "f":
-        if prod:
-            return rng.choice([0.5, 1.0, 2.0, -1.0], size=n).astype(dt)
+        if prod:  # bounded products: rare factors of 2 and 1/2 among +-1
+            return rng.choice([0.5, 1.0, 2.0, -1.0], p=[0.01, 0.49, 0.01, 0.49], size=n).astype(dt)
         return rng.uniform(-1, 1, size=n).astype(dt)
     if prod:
         return rng.choice([1, 3, 5, 7], size=n).astype(dt)  # odd: products never collapse to 0
@@ -289,3 +289,58 @@ def test_repeated_scans_reuse_workspace(device, oracle):
         want = oracle.scan_axis(x, [n], 0, reverse=k % 3 == 0, exclusive=k % 5 == 0)
         np.testing.assert_array_equal(device.download_owned(out), want)
     device.synchronize()  # no device-side error (look-back timeout) was raised
+
+
+@pytest.fixture
+def small_parts(monkeypatch):
+    """16 KiB parts for the chunked scan, so that a few million elements span
+    many chunks (the launcher reads the knob at every call)."""
+    monkeypatch.setenv("HEPH_SCAN_PART_KB", "16")
+    yield
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_chunked_scan_many_chunks(device, oracle, dt, small_parts):
+    rng = np.random.default_rng(123 + DTYPES.index(dt))
+    ops = CudaScanOps()
+    for n in [6_000_000, 6_062_080, 9_000_001]:
+        x = rand(dt, n, rng)
+        buf, out = device.upload(x), device.alloc_zeroed(dt, n)
+        for rev in (False, True):
+            for exc in (False, True):
+                ops.scan_axis_into(CumSumOp, device, StridedView(buf, Layout.c_contiguous([n])), 0, int(rev),
+                                   StridedView(out, Layout.c_contiguous([n])), exclusive=exc)
+                want = oracle.scan_axis(x, [n], 0, reverse=rev, exclusive=exc)
+                got = device.download_owned(out)
+                if np.dtype(dt).kind == "f":
+                    np.testing.assert_allclose(got.astype(np.float64), want.astype(np.float64), rtol=0,
+                                               atol=tol(dt, x))
+                else:
+                    np.testing.assert_array_equal(got, want, err_msg=f"n={n} rev={rev} exc={exc}")
+    device.synchronize()
+
+
+def test_chunked_scan_prod_u32(device, oracle, small_parts):
+    rng = np.random.default_rng(5)
+    n = 8_000_000
+    x = rand(np.uint32, n, rng, prod=True)
+    buf, out = device.upload(x), device.alloc_zeroed(np.uint32, n)
+    CudaScanOps().scan_axis_into(CumProdOp, device, StridedView(buf, Layout.c_contiguous([n])), 0, 0,
+                                 StridedView(out, Layout.c_contiguous([n])))
+    np.testing.assert_array_equal(device.download_owned(out), oracle.scan_axis(x, [n], 0, op=1))
+
+
+@pytest.mark.parametrize("dt", [np.uint32, np.int64])
+def test_lookback_scan_long_line(device, oracle, dt, monkeypatch):
+    """The look-back kernel on a long line (the chunked kernel switched off)."""
+    monkeypatch.setenv("HEPH_SCAN_NO_CHUNKED", "1")
+    rng = np.random.default_rng(77)
+    n = 12_000_003
+    x = rand(dt, n, rng)
+    buf, out = device.upload(x), device.alloc_zeroed(dt, n)
+    for rev, exc in [(False, True), (True, False)]:
+        CudaScanOps().scan_axis_into(CumSumOp, device, StridedView(buf, Layout.c_contiguous([n])), 0, int(rev),
+                                     StridedView(out, Layout.c_contiguous([n])), exclusive=exc)
+        np.testing.assert_array_equal(device.download_owned(out),
+                                      oracle.scan_axis(x, [n], 0, reverse=rev, exclusive=exc))
+    device.synchronize()
