@@ -12,7 +12,7 @@
 //   parts.  Each CTA keeps three of its parts in shared memory, filled by TMA
 //   bulk copies, so ~100 KiB of input per SM is always in flight.  Per chunk
 //   it reduces its next part, publishes the part's total, folds the totals of
-//   the parts before its own (read one chunk ahead), scans its part from
+//   the parts before its own, scans its part from
 //   shared memory and streams the results out.  HBM moves each element
 //   exactly twice and the only cross-CTA exchange is G totals per chunk.
 // * scan_lookback_kernel — contiguous lines too short (or too many) for the
@@ -42,7 +42,7 @@ constexpr uint32_t kPolls = 1u << 20;        // bounded waits on other CTAs
 constexpr int kLookbackVectors = 8;          // look-back tile: 8 x 128-bit per thread (32 KiB)
 constexpr int kChunkVectors = 4;             // chunked kernel tile: 4 x 128-bit per thread (16 KiB)
 constexpr int kChunkMaxBuffers = 6;          // part buffers per CTA of the chunked scan
-constexpr int kChunkMaxPartsPerThread = 4;   // chunked grids have at most 4 x 256 CTAs
+constexpr int kChunkMaxPartsPerThread = 2;   // chunked grids have at most 2 x 256 CTAs
 
 // Scan status workspace, per entry (tile or part): a packed 64-bit word for
 // 4-byte types, then two 8-byte value arrays and a 32-bit flag array for
@@ -240,9 +240,22 @@ __device__ __forceinline__ void load_tile_scalar(const T *src, uint64_t valid, i
         }
 }
 
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void st_policy(uint4 *p, uint4 v, uint64_t pol) {
+    asm volatile("st.global.L1::no_allocate.L2::cache_hint.v4.u32 [%0], {%1,%2,%3,%4}, %5;" ::"l"(p), "r"(v.x),
+                 "r"(v.y), "r"(v.z), "r"(v.w), "l"(pol)
+                 : "memory");
+}
+
+// Stores a tile: 128-bit stores for a full tile (store_mode 0: streaming
+// .cs hint, 1: L2 evict-first policy, 2: plain), element stores otherwise.
 template <typename T, int JV>
 __device__ __forceinline__ void store_tile(T *dst, uint64_t valid, bool full, int base,
-                                           const T (&y)[JV][ScanShape<T, JV>::V]) {
+                                           const T (&y)[JV][ScanShape<T, JV>::V], int store_mode = 0) {
     constexpr int V = ScanShape<T, JV>::V;
     if (full) {
 #pragma unroll
@@ -250,7 +263,10 @@ __device__ __forceinline__ void store_tile(T *dst, uint64_t valid, bool full, in
             Vec16<T> e;
 #pragma unroll
             for (int c = 0; c < V; ++c) e.e[c] = y[j][c];
-            st_stream(reinterpret_cast<uint4 *>(dst + base + j * 32 * V), as_uint4(e));
+            uint4 *q = reinterpret_cast<uint4 *>(dst + base + j * 32 * V);
+            if (store_mode == 1) st_policy(q, as_uint4(e), l2_policy_evict_first());
+            else if (store_mode == 2) *q = as_uint4(e);
+            else st_stream(q, as_uint4(e));
         }
     } else {
 #pragma unroll
@@ -367,6 +383,7 @@ template <typename T> struct ChunkParams {
     unsigned int *err;
     int reverse, exclusive;
     int buffers;       // shared-memory part buffers per CTA (2..kChunkMaxBuffers)
+    int store_mode;    // see store_tile
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -400,6 +417,51 @@ __device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, unsign
     if (threadIdx.x == 0) raise_device_error(err, DEVERR_BULK_TIMEOUT);
 }
 
+// Element range [lo, hi) of CTA b's part of logical chunk c.
+template <typename T>
+__device__ __forceinline__ void chunk_part_range(const ChunkParams<T> &p, int b, uint64_t c, uint64_t &lo,
+                                                 uint64_t &hi) {
+    const uint64_t pc = p.reverse ? p.nchunks - 1 - c : c;
+    lo = min(p.len, pc * p.chunk + (uint64_t)b * p.part);
+    hi = min(p.len, lo + p.part);
+}
+
+// Thread 0: start the bulk copy of CTA b's part of logical chunk c into its
+// buffer (full parts only; a ragged final part is read from global memory).
+template <typename T>
+__device__ __forceinline__ void chunk_stage_in(const ChunkParams<T> &p, int b, uint64_t c, T *buf, uint64_t *bar) {
+    uint64_t lo, hi;
+    chunk_part_range(p, b, c, lo, hi);
+    const int k = (int)(c % p.buffers);
+    if (hi - lo == p.part) bulk_load(buf + k * p.part, p.in + lo, (uint32_t)(p.part * sizeof(T)), &bar[k]);
+}
+
+// Step 1 of a chunk: total of CTA b's part of logical chunk c, published.
+template <typename T, int OP>
+__device__ __forceinline__ void chunk_reduce_part(const ChunkParams<T> &p, int b, uint64_t c, const T *buf,
+                                                  uint64_t *bar, uint32_t &phases, T *s_red) {
+    constexpr int V = Vec16<T>::V;
+    uint64_t lo, hi;
+    chunk_part_range(p, b, c, lo, hi);
+    const uint64_t n = hi - lo;
+    T acc = identity<T, OP>();
+    if (n == p.part) {
+        const int k = (int)(c % p.buffers);
+        mbar_wait(&bar[k], (phases >> k) & 1u, p.err);
+        phases ^= 1u << k;
+        const uint4 *v = reinterpret_cast<const uint4 *>(buf + k * p.part);
+        for (uint64_t q = threadIdx.x; q < n / V; q += kScanThreads) {
+            Vec16<T> e = as_elems<T>(v[q]);
+#pragma unroll
+            for (int t = 0; t < V; ++t) acc = combine<T, OP>(acc, e.e[t]);
+        }
+    } else {
+        for (uint64_t e = lo + threadIdx.x; e < hi; e += kScanThreads) acc = combine<T, OP>(acc, p.in[e]);
+    }
+    acc = block_fold<T, OP, kScanThreads>(acc, s_red);
+    if (threadIdx.x == 0) publish(p.status, c * gridDim.x + b, kStatePrefix, acc);
+}
+
 template <typename T, int OP, int JV>
 __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkParams<T> p) {
     using S = ScanShape<T, JV>;
@@ -417,75 +479,18 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
     const int base = tile_base_pos<T, JV>(warp, lane);
     uint32_t phases = 0;
 
-    auto part_range = [&](uint64_t c, uint64_t &lo, uint64_t &hi) {
-        const uint64_t pc = rev ? p.nchunks - 1 - c : c;
-        lo = min(p.len, pc * p.chunk + (uint64_t)b * p.part);
-        hi = min(p.len, lo + p.part);
-    };
-    // Thread 0: start the bulk copy of this CTA's part of logical chunk c
-    // (full parts only; a ragged final part is read from global memory).
-    auto stage_in = [&](uint64_t c) {
-        uint64_t lo, hi;
-        part_range(c, lo, hi);
-        if (hi - lo == p.part)
-            bulk_load(buf + (c % NB) * p.part, p.in + lo, (uint32_t)(p.part * sizeof(T)), &bar[c % NB]);
-    };
-
-    // Step 1: total of this CTA's part of logical chunk c.
-    auto reduce_part = [&](uint64_t c) {
-        uint64_t lo, hi;
-        part_range(c, lo, hi);
-        const uint64_t n = hi - lo;
-        T acc = identity<T, OP>();
-        if (n == p.part) {
-            const int k = (int)(c % NB);
-            mbar_wait(&bar[k], (phases >> k) & 1u, p.err);
-            phases ^= 1u << k;
-            const uint4 *v = reinterpret_cast<const uint4 *>(buf + k * p.part);
-            for (uint64_t q = threadIdx.x; q < n / V; q += kScanThreads) {
-                Vec16<T> e = as_elems<T>(v[q]);
-#pragma unroll
-                for (int t = 0; t < V; ++t) acc = combine<T, OP>(acc, e.e[t]);
-            }
-        } else {
-            for (uint64_t e = lo + threadIdx.x; e < hi; e += kScanThreads) acc = combine<T, OP>(acc, p.in[e]);
-        }
-        acc = block_fold<T, OP, kScanThreads>(acc, s_red);
-        if (threadIdx.x == 0) publish(p.status, c * G + b, kStatePrefix, acc);
-    };
-
-    // Status words of chunk c's part totals (4-byte types), loaded one chunk
-    // ahead without waiting; validated when the totals are needed.
-    unsigned long long pf[kChunkMaxPartsPerThread];
-    auto prefetch = [&](uint64_t c) {
-        if constexpr (sizeof(T) == 4) {
-#pragma unroll
-            for (int i = 0; i < kChunkMaxPartsPerThread; ++i) {
-                const int q = threadIdx.x + i * kScanThreads;
-                if (q < G)
-                    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];"
-                                 : "=l"(pf[i])
-                                 : "l"(p.status.packed + c * G + q)
-                                 : "memory");
-            }
-        }
-    };
-
     if (threadIdx.x == 0) {
         for (int k = 0; k < NB; ++k) mbar_init(&bar[k], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int k = 0; k < NB && (uint64_t)k < p.nchunks; ++k) stage_in(k);
+        for (int k = 0; k < NB && (uint64_t)k < p.nchunks; ++k) chunk_stage_in(p, b, k, buf, bar);
     }
     __syncthreads();
 
     T carry = p.carry ? *p.carry : identity<T, OP>();
-    if (p.nchunks > 0) {
-        reduce_part(0);
-        prefetch(0);
-    }
+    if (p.nchunks > 0) chunk_reduce_part<T, OP>(p, b, 0, buf, bar, phases, s_red);
     int parity = 0;
     for (uint64_t c = 0; c < p.nchunks; ++c) {
-        if (c + 1 < p.nchunks) reduce_part(c + 1);
+        if (c + 1 < p.nchunks) chunk_reduce_part<T, OP>(p, b, c + 1, buf, bar, phases, s_red);
 
         // Step 2: the part totals of chunk c.
         T before = identity<T, OP>(), total = identity<T, OP>();
@@ -494,13 +499,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
             const int q = threadIdx.x + i * kScanThreads;
             if (q >= G) break;
             T v = identity<T, OP>();
-            bool ok;
-            if constexpr (sizeof(T) == 4) {
-                v = bitcast<T>((uint32_t)(pf[i] >> 32));
-                ok = ((uint32_t)pf[i] >> 2) == p.status.epoch;
-            } else {
-                ok = read_status(p.status, c * G + q, v) != kStateInvalid;
-            }
+            bool ok = read_status(p.status, c * G + q, v) != kStateInvalid;
             uint32_t polls = 0;
             while (!ok) {
                 if (++polls > kPolls) {
@@ -516,13 +515,12 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
         }
         before = block_fold<T, OP, kScanThreads>(before, s_red);
         total = block_fold<T, OP, kScanThreads>(total, s_red2);
-        if (c + 1 < p.nchunks) prefetch(c + 1);
         T run = combine<T, OP>(carry, before);
         carry = combine<T, OP>(carry, total);
 
         // Step 3: scan the part in tiles, in logical order.
         uint64_t lo, hi;
-        part_range(c, lo, hi);
+        chunk_part_range(p, b, c, lo, hi);
         const bool staged = hi - lo == p.part;  // landed: step 1 waited for it
         const T *src = staged ? buf + (c % NB) * p.part : p.in + lo;
         const uint64_t ntiles = (hi - lo + TILE - 1) / TILE;
@@ -540,11 +538,11 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
             T y[JV][V];
             tile_outputs<T, OP, JV>(x, r, run, rev, excl, y);
             run = combine<T, OP>(run, r.agg);
-            store_tile<T, JV>(p.out + lo + start, valid, full, base, y);
+            store_tile<T, JV>(p.out + lo + start, valid, full, base, y, p.store_mode);
         }
         // Every thread is done with buffer c%NB: refill it with chunk c+NB.
         __syncthreads();
-        if (threadIdx.x == 0 && c + NB < p.nchunks) stage_in(c + NB);
+        if (threadIdx.x == 0 && c + NB < p.nchunks) chunk_stage_in(p, b, c + NB, buf, bar);
     }
 }
 
@@ -642,6 +640,7 @@ static bool launch_chunked(Device *dev, cudaStream_t stream, const T *in, T *out
     cp.reverse = reverse;
     cp.exclusive = exclusive;
     cp.buffers = nb;
+    cp.store_mode = scan_knob("HEPH_SCAN_STORE", 1);
     *st = status_for(dev, stream, cp.nchunks * G, &cp.status);
     if (*st != HEPH_OK) return true;
     void *args[] = {&cp};
