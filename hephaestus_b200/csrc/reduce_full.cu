@@ -198,3 +198,109 @@ heph_status launch_reduce_full(Device *dev, cudaStream_t stream, int op, heph_dt
 }
 
 }  // namespace heph
+
+// ------------------------------------------- allocation-free full reduction
+//
+// For callers that cannot allocate device memory at call time — an embedder
+// that runs inside a fixed memory budget or hands this library only the
+// buffers it owns, or code whose allocator must not be re-entered from the
+// call site.  The scratch the reduction needs (one partial per CTA plus the
+// last-CTA ticket) lives in this file-scope array, which every GPU that loads
+// the library holds for the life of the process.
+
+namespace heph {
+namespace {
+
+constexpr int kStaticPartials = 2048;  // CTA partials (8 bytes each) the array holds
+// [0, 16 KiB): partials of up to kStaticPartials CTAs; then the ticket.
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticPartials * 8 + 256];
+
+// Device address of g_static_scratch, looked up once per device.
+std::mutex g_static_mu;
+void *g_static_addr[256] = {};
+
+heph_status static_scratch_address(void **out) {
+    int dev = 0;
+    HEPH_CUDA_TRY(cudaGetDevice(&dev), HEPH_DEVICE_UNAVAILABLE, "cudaGetDevice");
+    if (dev < 0 || dev >= 256) return fail(HEPH_DEVICE_UNAVAILABLE, "device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_addr[dev]) {
+        void *p = nullptr;
+        HEPH_CUDA_TRY(cudaGetSymbolAddress(&p, g_static_scratch), HEPH_DEVICE_UNAVAILABLE,
+                      "static scratch address lookup");
+        g_static_addr[dev] = p;
+    }
+    *out = g_static_addr[dev];
+    return HEPH_OK;
+}
+
+template <typename Tin, typename Tacc, int OP>
+heph_status launch_static_typed(const void *in_v, uint64_t count, void *out_v, cudaStream_t stream, int sm_count) {
+    const Tin *in = static_cast<const Tin *>(in_v);
+    Tacc *out = static_cast<Tacc *>(out_v);
+    if (count == 0) {
+        write_identity_kernel<Tacc, OP><<<1, 1, 0, stream>>>(out);
+        HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "full reduction launch");
+        return HEPH_OK;
+    }
+    const uint64_t per_cta = (uint64_t)kReduceThreads * kReduceUnroll * (16 / sizeof(Tin));
+    const uint64_t want = (count + per_cta - 1) / per_cta;
+    const uint64_t cap = (uint64_t)sm_count * (2048 / kReduceThreads);
+    const uint64_t grid = std::max<uint64_t>(1, std::min(want, cap));
+    if (grid > (uint64_t)kStaticPartials)
+        return fail(HEPH_INVALID_CONFIGURATION,
+                    "allocation-free reduction needs " + std::to_string(grid) +
+                        " CTA partials but its static scratch holds at most " + std::to_string(kStaticPartials));
+    void *scratch = nullptr;
+    heph_status st = static_scratch_address(&scratch);
+    if (st != HEPH_OK) return st;
+    Tacc *partials = static_cast<Tacc *>(scratch);
+    unsigned int *ticket = reinterpret_cast<unsigned int *>(static_cast<char *>(scratch) + kStaticPartials * 8);
+    // The ticket must start at zero; a previous call leaves it at zero, but
+    // clear it in stream order so an earlier failed launch cannot poison it.
+    HEPH_CUDA_TRY(cudaMemsetAsync(ticket, 0, sizeof(unsigned int), stream), HEPH_DISPATCH_FAILED,
+                  "static scratch clear");
+    reduce_dense_kernel<Tin, Tacc, OP><<<(unsigned)grid, kReduceThreads, 0, stream>>>(in, count, out, partials, ticket);
+    HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "full reduction launch");
+    return HEPH_OK;
+}
+
+template <typename Tin, typename Tacc>
+heph_status launch_static_op(int op, const void *in, uint64_t count, void *out, cudaStream_t s, int sms) {
+    switch (op) {
+        case OP_SUM: return launch_static_typed<Tin, Tacc, OP_SUM>(in, count, out, s, sms);
+        case OP_PROD: return launch_static_typed<Tin, Tacc, OP_PROD>(in, count, out, s, sms);
+        case OP_MIN: return launch_static_typed<Tin, Tacc, OP_MIN>(in, count, out, s, sms);
+        case OP_MAX: return launch_static_typed<Tin, Tacc, OP_MAX>(in, count, out, s, sms);
+    }
+    return fail(HEPH_INVALID_CONFIGURATION, "full reduction supports sum, prod, min and max");
+}
+
+}  // namespace
+}  // namespace heph
+
+using namespace heph;
+
+extern "C" heph_status heph_reduce_full_noalloc(heph_op op, heph_dtype in_dtype, heph_dtype out_dtype,
+                                                const void *in, uint64_t count, void *out, heph_stream stream) {
+    if ((count && !in) || !out) return fail(HEPH_INVALID_CONFIGURATION, "null device pointer");
+    if ((reinterpret_cast<uintptr_t>(in) % (dtype_size(in_dtype) ? dtype_size(in_dtype) : 1)) != 0 ||
+        (reinterpret_cast<uintptr_t>(out) % (dtype_size(out_dtype) ? dtype_size(out_dtype) : 1)) != 0)
+        return fail(HEPH_INVALID_CONFIGURATION, "device pointers must be aligned to their element size");
+    int dev = 0, sms = 0;
+    HEPH_CUDA_TRY(cudaGetDevice(&dev), HEPH_DEVICE_UNAVAILABLE, "cudaGetDevice");
+    HEPH_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), HEPH_DEVICE_UNAVAILABLE,
+                  "device query");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (in_dtype == out_dtype) {
+        return dispatch_dtype(in_dtype, [&]<typename T>() {
+            return launch_static_op<T, T>((int)op, in, count, out, s, sms);
+        });
+    }
+    if (in_dtype == HEPH_I32 && out_dtype == HEPH_I64)
+        return launch_static_op<int32_t, int64_t>((int)op, in, count, out, s, sms);
+    if (in_dtype == HEPH_F32 && out_dtype == HEPH_F64)
+        return launch_static_op<float, double>((int)op, in, count, out, s, sms);
+    return fail(HEPH_INVALID_CONFIGURATION,
+                "full reduction output type must match the input type or widen it (i32->i64, f32->f64)");
+}

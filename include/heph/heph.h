@@ -319,6 +319,32 @@ heph_status heph_scan_seeded(heph_device *device, heph_op op, int exclusive,
                              const heph_buffer *carry, uint64_t carry_offset,
                              heph_stream stream);
 
+/* ------------------------------------------ allocation-free full reduction */
+
+/* No counterpart in the reference: an extra entry point for callers that
+ * cannot allocate device memory when they call in (a host that runs inside a
+ * fixed memory budget or owns every device buffer itself, or code that must
+ * not re-enter an allocator from the call site).  heph_reduce_full may
+ * allocate its workspace from the stream-ordered pool on first use per
+ * stream; this variant allocates nothing and needs no heph_device.
+ *
+ * Reduces `count` contiguous elements at the device pointer `in` (dtype
+ * in_dtype, current CUDA device) into the single element `*out` (out_dtype ==
+ * in_dtype, or the widening pairs I32->I64, F32->F64), op SUM/PROD/MIN/MAX,
+ * enqueued on `stream` (NULL = the legacy default stream).  Result identical
+ * in algorithm to heph_reduce_full on a dense view.
+ *
+ * Scratch: a static 16 KiB + 256 B device array inside the library (every GPU
+ * that loads the library keeps it until the process exits) that holds one
+ * partial per CTA for at most 2048 CTAs; a launch that would need more is
+ * rejected with HEPH_INVALID_CONFIGURATION.  The first call on each device
+ * looks up that array's device address (no allocation); make that first call
+ * before any stream capture.  All calls share the one array, so calls whose
+ * kernels overlap on the GPU (different streams, or several host threads)
+ * race and must be serialised by the caller. */
+heph_status heph_reduce_full_noalloc(heph_op op, heph_dtype in_dtype, heph_dtype out_dtype,
+                                     const void *in, uint64_t count, void *out, heph_stream stream);
+
 #ifdef __cplusplus
 }
 #endif
