@@ -1,0 +1,36 @@
+"""Partitioned 1-D scan and reduce over 2+ GPUs (NCCL all-gather of per-rank
+totals), checked bit-exactly against the oracle on the whole buffer.  Runs the
+ranks as child processes (tests/dist_worker.py); skipped with fewer than two
+GPUs."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_partitioned_scan_and_reduce(tmp_path, oracle):
+    import torch
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    world = min(world, 4)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", "--master-port", "29533",
+           os.path.join(ROOT, "tests", "dist_worker.py"), str(tmp_path)]
+    res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stderr[-3000:]
+    cat = lambda name: np.concatenate([np.load(tmp_path / f"{name}_{r}.npy") for r in range(world)])  # noqa: E731
+    xi, xu = cat("in_i32"), cat("in_u32")
+    np.testing.assert_array_equal(xi, oracle.generate(oracle.GEN_I32_PM1000, 4, xi.size))
+    np.testing.assert_array_equal(xu, oracle.generate(oracle.GEN_U32_LOW4, 1, xu.size))
+    np.testing.assert_array_equal(cat("scan_i32"), oracle.scan_axis(xi, [xi.size], 0))
+    np.testing.assert_array_equal(cat("scan_u32"), oracle.scan_axis(xu, [xu.size], 0, exclusive=True))
+    for r in range(world):
+        assert np.load(tmp_path / f"sum_{r}.npy")[0] == int(xi.astype(np.int64).sum())
+        assert np.load(tmp_path / f"max_{r}.npy")[0] == xu.max()
