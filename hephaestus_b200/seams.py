@@ -157,6 +157,18 @@ class CudaScanOps:
                                            ctypes.byref(ol), ctypes.byref(h)))
         return Prepared(h.value, (input, output))
 
+    def scan_host(self, op, device, host_in, host_out, exclusive: bool = False, chunk_elems: int = 0):
+        """[EXT] Scan a host array into a host array with the transfers
+        overlapped (heph_scan_host); both arrays C-contiguous, same dtype."""
+        from .core import InvalidConfiguration, dtype_code
+        if host_in.dtype != host_out.dtype or host_in.size != host_out.size:
+            raise InvalidConfiguration("host input and output must have the same type and length")
+        if not (host_in.flags.c_contiguous and host_out.flags.c_contiguous):
+            raise InvalidConfiguration("host arrays must be C-contiguous")
+        check(N.lib.heph_scan_host(device.handle, op.code, int(bool(exclusive)), dtype_code(host_in.dtype),
+                                   host_in.ctypes.data_as(ctypes.c_void_p),
+                                   host_out.ctypes.data_as(ctypes.c_void_p), host_in.size, int(chunk_elems)))
+
     def dispatch_scan(self, device, prepared: Prepared, stream=None):
         _dispatch(device, prepared, stream)
 

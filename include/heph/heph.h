@@ -319,6 +319,20 @@ heph_status heph_scan_seeded(heph_device *device, heph_op op, int exclusive,
                              const heph_buffer *carry, uint64_t carry_offset,
                              heph_stream stream);
 
+/* ------------------------------------------- [EXT] host-buffer scan pipeline */
+
+/* Forward scan (op SUM/PROD, inclusive or exclusive) of `count` contiguous
+ * elements in HOST memory into host memory — the composition upload ->
+ * scan_axis_into -> download of the reference (core device.rs:135, scan.rs:219,
+ * device.rs:147) with the three phases overlapped: chunks of `chunk_elems`
+ * (0 = 64 MiB worth) flow through three device slots, host->device copies,
+ * seeded device scans and device->host copies running concurrently on two
+ * copy engines and the device's stream.  Returns when host_out is complete.
+ * Staging comes from the device's stream-ordered pool.  Pinned host memory
+ * (heph_host_alloc_pinned) is needed for the copies to overlap. */
+heph_status heph_scan_host(heph_device *device, heph_op op, int exclusive, heph_dtype dtype,
+                           const void *host_in, void *host_out, uint64_t count, uint64_t chunk_elems);
+
 /* ------------------------------------------ allocation-free full reduction */
 
 /* No counterpart in the reference: an extra entry point for callers that

@@ -344,3 +344,19 @@ def test_lookback_scan_long_line(device, oracle, dt, monkeypatch):
         np.testing.assert_array_equal(device.download_owned(out),
                                       oracle.scan_axis(x, [n], 0, reverse=rev, exclusive=exc))
     device.synchronize()
+
+
+@pytest.mark.parametrize("dt,exc", [(np.uint32, True), (np.int32, False), (np.float32, False), (np.int64, True)])
+def test_scan_host_pipeline(device, oracle, dt, exc):
+    """heph_scan_host: chunked, transfer-overlapped scan of host arrays."""
+    rng = np.random.default_rng(31)
+    ops = CudaScanOps()
+    for n, chunk in [(1, 0), (1000, 7), (100_003, 4096), (3_000_001, 1 << 20), (5_000_000, 0)]:
+        x = rand(dt, n, rng)
+        y = np.empty_like(x)
+        ops.scan_host(CumSumOp, device, x, y, exclusive=exc, chunk_elems=chunk)
+        want = oracle.scan_axis(x, [n], 0, exclusive=exc)
+        if np.dtype(dt).kind == "f":
+            np.testing.assert_allclose(y.astype(np.float64), want.astype(np.float64), rtol=0, atol=tol(dt, x))
+        else:
+            np.testing.assert_array_equal(y, want, err_msg=f"n={n} chunk={chunk}")
