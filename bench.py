@@ -42,7 +42,7 @@ CONFIGS = {
                      "(64 rotating buffers, 256 MiB > L2)", n=1 << 20, dtype="f32",
             kernel="reduce_dense_kernel", bytes_per_elem=4),
     2: dict(workload="u32 exclusive prefix scan over 2^28 elements per GPU, h&15 seed 1",
-            n=1 << 28, dtype="u32", kernel="scan_lookback_kernel", bytes_per_elem=8),
+            n=1 << 28, dtype="u32", kernel="scan_chunked_kernel", bytes_per_elem=8),
     3: dict(workload="f32 row-wise max + argmax over [65536 x 4096] row-major, N(0,1) seed 2, "
                      "~1% injected exact ties", rows=65536, cols=4096, dtype="f32",
             kernel="row_reduce_kernel"),
@@ -50,7 +50,7 @@ CONFIGS = {
             rows=4096, cols=65536, dtype="f64", kernel="col_reduce_kernel"),
     5: dict(workload="i32 inclusive scan + i64-accumulated sum over 2^32 elements (16 GiB) "
                      "U{-1000..1000} seed 4, partitioned 1-D across the GPUs",
-            n=1 << 32, dtype="i32", kernel="scan_lookback_kernel"),
+            n=1 << 32, dtype="i32", kernel="scan_chunked_kernel"),
 }
 
 
@@ -443,11 +443,18 @@ def main():
     # ---------------- CPU baseline (rank 0, N=1 only) -------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        from oracle import host_ref as oracle
-        oracle.build()
-        v, cores, desc = cpu_sample(args.config, cfg, oracle, seconds=10.0)
-        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-               "sample": desc + " (oracle restatement of the host reference semantics, OpenMP)"}
+        # The reference arm in a fresh process (no CUDA / torch runtime in it),
+        # so the baseline is measured exactly as the reference line is.
+        env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+        res = subprocess.run([sys.executable, os.path.abspath(__file__), "--impl", "reference", "--config",
+                              str(args.config), "--steps", "2", "--warmup", "1"],
+                             capture_output=True, text=True, env=env, timeout=600)
+        try:
+            ref = json.loads(res.stdout.strip().splitlines()[-1])
+            cpu = dict(ref["cpu_baseline"])
+        except Exception:
+            cpu = {"value": None, "unit": "GB/s", "cores": None, "kind": "port",
+                   "sample": "reference arm failed: " + res.stderr[-200:]}
 
     if rank == 0:
         line = {

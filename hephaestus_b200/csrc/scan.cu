@@ -114,7 +114,8 @@ __device__ __forceinline__ uint32_t read_status(const StatusView &s, uint64_t id
 // ------------------------------------------------------------ tile scans
 
 // Inclusive warp scan in logical lane order (descending lanes when `rev`).
-template <typename T, int OP> __device__ __forceinline__ T warp_scan(T v, int lane, bool rev) {
+template <typename T, int OP, bool REV> __device__ __forceinline__ T warp_scan(T v, int lane) {
+    constexpr bool rev = REV;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
         const T o = rev ? shfl_down(v, d) : shfl_up(v, d);
@@ -142,9 +143,9 @@ template <typename T, int JV> struct TileScan {
     T wpre, agg;
 };
 
-template <typename T, int OP, int JV>
-__device__ __forceinline__ void tile_local_scan(T (&x)[JV][ScanShape<T, JV>::V], bool rev, T *s_warp,
-                                                TileScan<T, JV> &r) {
+template <typename T, int OP, int JV, bool REV>
+__device__ __forceinline__ void tile_local_scan(T (&x)[JV][ScanShape<T, JV>::V], T *s_warp, TileScan<T, JV> &r) {
+    constexpr bool rev = REV;
     constexpr int V = ScanShape<T, JV>::V, J = JV;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     T tt[J];
@@ -165,7 +166,7 @@ __device__ __forceinline__ void tile_local_scan(T (&x)[JV][ScanShape<T, JV>::V],
 #pragma unroll
     for (int jl = 0; jl < J; ++jl) {
         const int jp = rev ? J - 1 - jl : jl;
-        const T inc = warp_scan<T, OP>(tt[jp], lane, rev);
+        const T inc = warp_scan<T, OP, REV>(tt[jp], lane);
         T exc = rev ? shfl_down(inc, 1) : shfl_up(inc, 1);
         if (first_lane) exc = identity<T, OP>();
         const T tot = shfl_idx(inc, rev ? 0 : 31);
@@ -185,10 +186,10 @@ __device__ __forceinline__ void tile_local_scan(T (&x)[JV][ScanShape<T, JV>::V],
 }
 
 // Final values of the tile given the exclusive prefix of the whole tile.
-template <typename T, int OP, int JV>
+template <typename T, int OP, int JV, bool REV, bool EXCL>
 __device__ __forceinline__ void tile_outputs(const T (&x)[JV][ScanShape<T, JV>::V], const TileScan<T, JV> &r,
-                                             T tile_prefix, bool rev, bool exclusive,
-                                             T (&y)[JV][ScanShape<T, JV>::V]) {
+                                             T tile_prefix, T (&y)[JV][ScanShape<T, JV>::V]) {
+    constexpr bool rev = REV, exclusive = EXCL;
     constexpr int V = ScanShape<T, JV>::V;
     const T thread_base = combine<T, OP>(tile_prefix, r.wpre);
 #pragma unroll
@@ -326,14 +327,14 @@ __device__ T lookback(const LookbackParams<T> &p, uint64_t tile, uint64_t line_f
 }
 
 // One tile per CTA; tiles of a line are numbered in scan order.
-template <typename T, int OP, bool VEC, int JV>
+template <typename T, int OP, bool VEC, int JV, bool REV, bool EXCL>
 __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const LookbackParams<T> p) {
     using S = ScanShape<T, JV>;
     constexpr int V = S::V, TILE = S::TILE;
     __shared__ T s_warp[kScanWarps];
     __shared__ T s_prefix;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const bool rev = p.reverse != 0;
+    constexpr bool rev = REV;
     const uint64_t tile = blockIdx.x;
     const uint64_t line = tile / p.tiles_per_line;
     const uint64_t t_in_line = tile - line * p.tiles_per_line;
@@ -349,7 +350,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const Lookb
     if (full) load_tile_vec<T, JV>(lin + start, base, x, true);
     else load_tile_scalar<T, OP, JV>(lin + start, valid, base, x);
     TileScan<T, JV> r;
-    tile_local_scan<T, OP, JV>(x, rev, s_warp, r);
+    tile_local_scan<T, OP, JV, REV>(x, s_warp, r);
 
     if (warp == 0) {
         T tp;
@@ -365,7 +366,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const Lookb
     }
     __syncthreads();
     T y[JV][V];
-    tile_outputs<T, OP, JV>(x, r, s_prefix, rev, p.exclusive != 0, y);
+    tile_outputs<T, OP, JV, REV, EXCL>(x, r, s_prefix, y);
     store_tile<T, JV>(lout + start, valid, full, base, y);
 }
 
@@ -462,7 +463,7 @@ __device__ __forceinline__ void chunk_reduce_part(const ChunkParams<T> &p, int b
     if (threadIdx.x == 0) publish(p.status, c * gridDim.x + b, kStatePrefix, acc);
 }
 
-template <typename T, int OP, int JV>
+template <typename T, int OP, int JV, bool REV, bool EXCL>
 __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkParams<T> p) {
     using S = ScanShape<T, JV>;
     constexpr int V = S::V, TILE = S::TILE;
@@ -475,7 +476,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int G = gridDim.x, b = blockIdx.x;
     const int NB = p.buffers;
-    const bool rev = p.reverse != 0, excl = p.exclusive != 0;
+    constexpr bool rev = REV;
     const int base = tile_base_pos<T, JV>(warp, lane);
     uint32_t phases = 0;
 
@@ -533,10 +534,10 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
             if (full) load_tile_vec<T, JV>(src + start, base, x, false);
             else load_tile_scalar<T, OP, JV>(src + start, valid, base, x);
             TileScan<T, JV> r;
-            tile_local_scan<T, OP, JV>(x, rev, s_warp[parity], r);
+            tile_local_scan<T, OP, JV, REV>(x, s_warp[parity], r);
             parity ^= 1;
             T y[JV][V];
-            tile_outputs<T, OP, JV>(x, r, run, rev, excl, y);
+            tile_outputs<T, OP, JV, REV, EXCL>(x, r, run, y);
             run = combine<T, OP>(run, r.agg);
             store_tile<T, JV>(p.out + lo + start, valid, full, base, y, p.store_mode);
         }
@@ -571,7 +572,7 @@ __global__ void __launch_bounds__(256) scan_strided_kernel(const StridedScanPara
         const bool ok = q < p.len;
         const uint64_t idx = p.reverse ? p.len - 1 - q : q;
         const T x = ok ? p.in[ib + (int64_t)idx * p.in_r] : identity<T, OP>();
-        const T inc = warp_scan<T, OP>(x, lane, false);
+        const T inc = warp_scan<T, OP, false>(x, lane);
         T exc = shfl_up(inc, 1);
         if (lane == 0) exc = identity<T, OP>();
         if (ok) p.out[ob + (int64_t)idx * p.out_r] = combine<T, OP>(running, p.exclusive ? exc : inc);
@@ -607,7 +608,7 @@ static heph_status status_for(Device *dev, cudaStream_t stream, uint64_t entries
 
 // The chunked kernel for one long aligned line.  Returns false (nothing
 // launched) when the line is too short to give every CTA four parts.
-template <typename T, int OP>
+template <typename T, int OP, bool REV, bool EXCL>
 static bool launch_chunked(Device *dev, cudaStream_t stream, const T *in, T *out, uint64_t len, bool reverse,
                            bool exclusive, const T *carry, heph_status *st) {
     using S = ScanShape<T, kChunkVectors>;
@@ -616,7 +617,7 @@ static bool launch_chunked(Device *dev, cudaStream_t stream, const T *in, T *out
     const uint64_t part = std::max<uint64_t>(1, part_bytes / sizeof(T) / S::TILE) * S::TILE;
     const size_t smem = (size_t)nb * part * sizeof(T);
     if (smem > (200u << 10)) return false;
-    auto kernel = scan_chunked_kernel<T, OP, kChunkVectors>;
+    auto kernel = scan_chunked_kernel<T, OP, kChunkVectors, REV, EXCL>;
     int nb_sm = 0;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb_sm, kernel, kScanThreads, smem) != cudaSuccess ||
@@ -672,9 +673,16 @@ static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *
     std::lock_guard<std::mutex> lock(dev->mu);
     if (vec && pr.outer == 1 && !scan_knob("HEPH_SCAN_NO_CHUNKED", 0)) {
         heph_status st = HEPH_OK;
-        if (launch_chunked<T, OP>(dev, stream, in + pr.in_base, out + pr.out_base, pr.len, reverse, exclusive,
-                                  carry, &st))
-            return st;
+        bool launched;
+        const T *ci = in + pr.in_base;
+        T *co = out + pr.out_base;
+        if (reverse)
+            launched = exclusive ? launch_chunked<T, OP, true, true>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st)
+                                 : launch_chunked<T, OP, true, false>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st);
+        else
+            launched = exclusive ? launch_chunked<T, OP, false, true>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st)
+                                 : launch_chunked<T, OP, false, false>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st);
+        if (launched) return st;
     }
     const uint64_t tiles_per_line = (pr.len + S::TILE - 1) / S::TILE;
     const uint64_t tiles = tiles_per_line * pr.outer;
@@ -692,10 +700,18 @@ static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *
     p.err = dev->error_dev;
     p.reverse = reverse;
     p.exclusive = exclusive;
-    if (vec)
-        scan_lookback_kernel<T, OP, true, kLookbackVectors><<<(unsigned)tiles, kScanThreads, 0, stream>>>(p);
-    else
-        scan_lookback_kernel<T, OP, false, kLookbackVectors><<<(unsigned)tiles, kScanThreads, 0, stream>>>(p);
+    const dim3 grid((unsigned)tiles);
+    const int sel = (vec ? 4 : 0) | (reverse ? 2 : 0) | (exclusive ? 1 : 0);
+    switch (sel) {
+        case 0: scan_lookback_kernel<T, OP, false, kLookbackVectors, false, false><<<grid, kScanThreads, 0, stream>>>(p); break;
+        case 1: scan_lookback_kernel<T, OP, false, kLookbackVectors, false, true><<<grid, kScanThreads, 0, stream>>>(p); break;
+        case 2: scan_lookback_kernel<T, OP, false, kLookbackVectors, true, false><<<grid, kScanThreads, 0, stream>>>(p); break;
+        case 3: scan_lookback_kernel<T, OP, false, kLookbackVectors, true, true><<<grid, kScanThreads, 0, stream>>>(p); break;
+        case 4: scan_lookback_kernel<T, OP, true, kLookbackVectors, false, false><<<grid, kScanThreads, 0, stream>>>(p); break;
+        case 5: scan_lookback_kernel<T, OP, true, kLookbackVectors, false, true><<<grid, kScanThreads, 0, stream>>>(p); break;
+        case 6: scan_lookback_kernel<T, OP, true, kLookbackVectors, true, false><<<grid, kScanThreads, 0, stream>>>(p); break;
+        default: scan_lookback_kernel<T, OP, true, kLookbackVectors, true, true><<<grid, kScanThreads, 0, stream>>>(p); break;
+    }
     HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "scan launch");
     return HEPH_OK;
 }
