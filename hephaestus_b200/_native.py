@@ -94,6 +94,9 @@ SIGNATURES = [
     ("heph_prepare_scan_axis", _st, [_vp, _i, _i, _i, _vp, _lp, _u32, _vp, _lp, _pp]),
     ("heph_dispatch_prepared", _st, [_vp, _vp, _vp]),
     ("heph_prepared_free", _st, [_vp]),
+    ("heph_batch_create", _st, [_vp, ctypes.POINTER(ctypes.c_void_p), _u32, _pp]),
+    ("heph_batch_launch", _st, [_vp, _vp]),
+    ("heph_batch_free", _st, [_vp]),
     ("heph_comm_unique_id", _st, [ctypes.c_char_p]),
     ("heph_comm_init", _st, [_vp, ctypes.c_char_p, _i, _i, _pp]),
     ("heph_comm_destroy", _st, [_vp]),

@@ -727,3 +727,85 @@ extern "C" heph_status heph_prepared_free(heph_prepared *prepared) {
     delete prepared;
     return HEPH_OK;
 }
+
+// ----------------------------------------------------- prepared batches
+
+// A CUDA graph that replays a fixed list of prepared reductions with one
+// launch (submit_prepared_reduction_batch, hephaestus-cuda
+// application/prepared_reduction.rs:165; submit_prepared_axis_reduction_batch,
+// prepared_axis_reduction.rs:84).  Scans are not batchable: each scan launch
+// carries the epoch tag of its tile status, which a replayed graph would reuse.
+struct heph_batch {
+    heph_device *device = nullptr;
+    cudaStream_t capture = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+};
+
+extern "C" heph_status heph_batch_create(heph_device *device, const heph_prepared *const *items, uint32_t count,
+                                         heph_batch **out) {
+    if (!device || !out || (count && !items)) return fail(HEPH_INVALID_CONFIGURATION, "null argument");
+    *out = nullptr;
+    for (uint32_t i = 0; i < count; ++i) {
+        if (!items[i]) return fail(HEPH_INVALID_CONFIGURATION, "null prepared item");
+        if (items[i]->call.kind == Kind::Scan)
+            return fail(HEPH_INVALID_CONFIGURATION, "prepared scans cannot be batched; dispatch them directly");
+        if (items[i]->call.in->device != device)
+            return fail(HEPH_DISPATCH_FAILED, "prepared operands belong to another device");
+    }
+    heph_status st = bind(device);
+    if (st != HEPH_OK) return st;
+    heph_batch *b = new heph_batch();
+    b->device = device;
+    auto cleanup = [&](heph_status s) {
+        if (b->exec) cudaGraphExecDestroy(b->exec);
+        if (b->graph) cudaGraphDestroy(b->graph);
+        if (b->capture) cudaStreamDestroy(b->capture);
+        delete b;
+        return s;
+    };
+    if (cudaStreamCreateWithFlags(&b->capture, cudaStreamNonBlocking) != cudaSuccess)
+        return cleanup(cuda_fail(HEPH_DISPATCH_FAILED, cudaGetLastError(), "batch stream"));
+    // One eager pass sets up the capture stream's workspace, so that the
+    // captured launches allocate nothing.
+    for (uint32_t i = 0; i < count; ++i) {
+        st = run(device, items[i]->call, b->capture);
+        if (st != HEPH_OK) return cleanup(st);
+    }
+    if (cudaStreamSynchronize(b->capture) != cudaSuccess)
+        return cleanup(cuda_fail(HEPH_DISPATCH_FAILED, cudaGetLastError(), "batch warm-up"));
+    if (cudaStreamBeginCapture(b->capture, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        return cleanup(cuda_fail(HEPH_DISPATCH_FAILED, cudaGetLastError(), "batch capture"));
+    for (uint32_t i = 0; i < count && st == HEPH_OK; ++i) st = run(device, items[i]->call, b->capture);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(b->capture, &g);
+    b->graph = g;
+    if (st != HEPH_OK) return cleanup(st);
+    if (e != cudaSuccess) return cleanup(cuda_fail(HEPH_DISPATCH_FAILED, e, "batch capture"));
+    e = cudaGraphInstantiate(&b->exec, b->graph, 0);
+    if (e != cudaSuccess) return cleanup(cuda_fail(HEPH_DISPATCH_FAILED, e, "batch instantiate"));
+    *out = b;
+    return HEPH_OK;
+}
+
+extern "C" heph_status heph_batch_launch(heph_batch *batch, heph_stream stream) {
+    if (!batch) return fail(HEPH_INVALID_CONFIGURATION, "null batch");
+    heph_status st = bind(batch->device);
+    if (st != HEPH_OK) return st;
+    HEPH_CUDA_TRY(cudaGraphLaunch(batch->exec, resolve_stream(batch->device, stream)), HEPH_DISPATCH_FAILED,
+                  "batch launch");
+    return HEPH_OK;
+}
+
+extern "C" heph_status heph_batch_free(heph_batch *batch) {
+    if (!batch) return HEPH_OK;
+    cudaSetDevice(batch->device->ordinal);
+    if (batch->exec) cudaGraphExecDestroy(batch->exec);
+    if (batch->graph) cudaGraphDestroy(batch->graph);
+    if (batch->capture) {
+        cudaStreamSynchronize(batch->capture);
+        cudaStreamDestroy(batch->capture);
+    }
+    delete batch;
+    return HEPH_OK;
+}

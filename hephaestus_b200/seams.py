@@ -55,6 +55,39 @@ def _dispatch(device: CudaDevice, prepared: Prepared, stream=None):
     check(N.lib.heph_dispatch_prepared(device.handle, prepared._h, _stream(stream)))
 
 
+class Batch:
+    """Prepared reductions replayed as one CUDA graph (heph_batch_*)."""
+
+    def __init__(self, device: CudaDevice, items):
+        self.device = device
+        self._items = list(items)  # keep the prepared handles (and their operands) alive
+        arr = (ctypes.c_void_p * len(self._items))(*[it._h.value for it in self._items])
+        h = ctypes.c_void_p()
+        check(N.lib.heph_batch_create(device.handle, arr, len(self._items), ctypes.byref(h)))
+        self._h = h
+
+    def launch(self, stream=None):
+        check(N.lib.heph_batch_launch(self._h, _stream(stream)))
+
+    def free(self):
+        if self._h:
+            N.lib.heph_batch_free(self._h)
+            self._h = ctypes.c_void_p(0)
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def submit_prepared_batch(device: CudaDevice, items, stream=None) -> "Batch":
+    """Record `items` (prepared reductions) as a batch and launch it once."""
+    b = Batch(device, items)
+    b.launch(stream)
+    return b
+
+
 class CudaFullReductionOps:
     """``FullReductionOps<CudaDevice, T>``."""
 

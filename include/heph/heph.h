@@ -277,6 +277,19 @@ heph_status heph_dispatch_prepared(heph_device *device, const heph_prepared *pre
                                    heph_stream stream);
 heph_status heph_prepared_free(heph_prepared *prepared);
 
+/* Batch submission — submit_prepared_reduction_batch (hephaestus-cuda
+ * application/prepared_reduction.rs:165) and submit_prepared_axis_reduction_batch
+ * (prepared_axis_reduction.rs:84): a fixed list of prepared full / axis
+ * reductions recorded once as a CUDA graph and replayed with one launch per
+ * heph_batch_launch.  Creation dispatches every item once (setting up the
+ * workspace the graph uses).  Replays of one batch must not overlap on the GPU.
+ * Prepared scans are rejected (InvalidConfiguration). */
+typedef struct heph_batch heph_batch;
+heph_status heph_batch_create(heph_device *device, const heph_prepared *const *items, uint32_t count,
+                              heph_batch **out);
+heph_status heph_batch_launch(heph_batch *batch, heph_stream stream);
+heph_status heph_batch_free(heph_batch *batch);
+
 /* ---------------------------------- [EXT] partitioned 1-D multi-GPU path */
 
 /* One process per GPU.  Rank 0 creates the id, the caller ships it to the

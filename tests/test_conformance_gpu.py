@@ -165,3 +165,33 @@ def test_allocating_scan_conveniences(device):
     np.testing.assert_array_equal(got, [15, 15, 5, 48, 24, 6])
     empty = device.alloc_zeroed(np.int32, 0)
     assert len(S.cumprod(device, StridedView(empty, Layout.c_contiguous([2, 0])), 1)) == 0
+
+
+def test_prepared_batch_submission(device):
+    """contract.rs:693-735: prepared min/max over u32 (i % 17) submitted as a
+    batch; the batch replays its bound operands (rebind contract); prepared
+    scans are not batchable."""
+    host = (np.arange(1027) % 17).astype(np.uint32)
+    buf = device.upload(host)
+    lay, one = Layout.c_contiguous([1027]), Layout.c_contiguous([1])
+    mn, mx = device.alloc_zeroed(np.uint32, 1), device.alloc_zeroed(np.uint32, 1)
+    ops = CudaFullReductionOps()
+    pmin = ops.prepare_reduce_full(MinOp, device, StridedView(buf, lay), StridedView(mn, one))
+    pmax = ops.prepare_reduce_full(MaxOp, device, StridedView(buf, lay), StridedView(mx, one))
+    m2 = device.upload(np.arange(1, 13, dtype=np.uint32))
+    col = device.alloc_zeroed(np.uint32, 4)
+    pcol = CudaAxisReductionOps().prepare_reduce_axis_into(SumOp, device, StridedView(m2, Layout.c_contiguous([3, 4])),
+                                                           0, StridedView(col, Layout.c_contiguous([1, 4])))
+    batch = S.submit_prepared_batch(device, [pmin, pmax, pcol])
+    assert device.download_owned(mn)[0] == 0 and device.download_owned(mx)[0] == 16
+    np.testing.assert_array_equal(device.download_owned(col), [15, 18, 21, 24])
+    device.write_buffer(buf, host + 5)
+    device.write_buffer(m2, np.full(12, 2, np.uint32))
+    batch.launch()
+    assert device.download_owned(mn)[0] == 5 and device.download_owned(mx)[0] == 21
+    np.testing.assert_array_equal(device.download_owned(col), [6, 6, 6, 6])
+    out = device.alloc_zeroed(np.uint32, 1027)
+    pscan = CudaScanOps().prepare_scan_axis(CumSumOp, device, StridedView(buf, lay), 0, 0, StridedView(out, lay))
+    from hephaestus_b200 import InvalidConfiguration
+    with pytest.raises(InvalidConfiguration):
+        S.Batch(device, [pscan])
