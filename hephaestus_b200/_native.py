@@ -17,6 +17,7 @@ OK, ADAPTER_UNAVAILABLE, DEVICE_UNAVAILABLE, ALLOCATION_FAILED, LENGTH_MISMATCH,
 F32, F64, U32, I32, I64 = range(5)
 SUM, PROD, MIN, MAX, MEAN = range(5)
 FORWARD, REVERSE = 0, 1
+MAP_DOT, MAP_SUM, MAP_NORM_L1, MAP_NORM_L2, MAP_NORM_MAX = range(5)
 MAX_RANK = 4
 COMM_ID_BYTES = 128
 
@@ -88,6 +89,8 @@ SIGNATURES = [
     ("heph_reduce_full", _st, [_vp, _i, _vp, _lp, _vp, _lp, _vp]),
     ("heph_reduce_axis", _st, [_vp, _i, _vp, _lp, _u32, _vp, _lp, _vp]),
     ("heph_arg_reduce_axis", _st, [_vp, _i, _vp, _lp, _u32, _vp, _lp, _vp, _lp, _vp]),
+    ("heph_map_reduce_full", _st, [_vp, _i, _vp, _lp, _vp, _lp, _vp, _lp, _vp]),
+    ("heph_prepare_map_reduce_full", _st, [_vp, _i, _vp, _lp, _vp, _lp, _vp, _lp, _pp]),
     ("heph_scan_axis", _st, [_vp, _i, _i, _i, _vp, _lp, _u32, _vp, _lp, _vp]),
     ("heph_prepare_reduce_full", _st, [_vp, _i, _vp, _lp, _vp, _lp, _pp]),
     ("heph_prepare_reduce_axis", _st, [_vp, _i, _vp, _lp, _u32, _vp, _lp, _pp]),

@@ -479,7 +479,7 @@ extern "C" heph_status heph_host_free_pinned(void *ptr) {
 
 namespace {
 
-enum class Kind { Full, Axis, Arg, Scan };
+enum class Kind { Full, Axis, Arg, Scan, Map };
 
 struct Call {
     Kind kind;
@@ -493,8 +493,10 @@ struct Call {
     uint32_t axis = 0;
     bool reverse = false, exclusive = false, mean = false;
     bool noop = false;
-    uint64_t count = 0;  // full reductions
+    uint64_t count = 0;  // full and map reductions
     AxisProblem p{};     // axis reductions and scans
+    const heph_buffer *b = nullptr;  // second operand of a dot product
+    heph_layout b_l{};
 };
 
 heph_status check_buffers(const heph_device *device, const heph_buffer *in, const heph_layout *il,
@@ -563,6 +565,37 @@ heph_status plan_scan(heph_device *device, heph_op op, heph_scan_direction dir, 
     return plan_axis_scan(*il, in->len, *ol, out->len, axis, ranges_overlap(in, out), &c->noop, &c->p);
 }
 
+heph_status plan_map(heph_device *device, heph_map map, const heph_buffer *a, const heph_layout *al,
+                     const heph_buffer *b, const heph_layout *bl, heph_buffer *out, const heph_layout *ol, Call *c) {
+    heph_status st = check_buffers(device, a, al, out, ol);
+    if (st != HEPH_OK) return st;
+    if ((int)map < HEPH_MAP_DOT || (int)map > HEPH_MAP_NORM_MAX)
+        return fail(HEPH_INVALID_CONFIGURATION, "unknown map reduction");
+    if (out->dtype != a->dtype) return fail(HEPH_DISPATCH_FAILED, "map reduction output element type must match the input");
+    if (map == HEPH_MAP_NORM_L2 && a->dtype != HEPH_F32 && a->dtype != HEPH_F64)
+        return fail(HEPH_DISPATCH_FAILED, "norm_l2 requires a floating-point element type");
+    if (map == HEPH_MAP_DOT) {
+        if (!b || !bl) return fail(HEPH_INVALID_CONFIGURATION, "dot product needs two operands");
+        if (b->device != device) return fail(HEPH_DISPATCH_FAILED, "operand buffers belong to another device");
+        if (b->dtype != a->dtype) return fail(HEPH_DISPATCH_FAILED, "dot product operands must share an element type");
+        bool same = al->rank == bl->rank;
+        for (uint32_t d = 0; same && d < al->rank && d < HEPH_MAX_RANK; ++d) same = al->shape[d] == bl->shape[d];
+        if (!same)
+            return fail(HEPH_DISPATCH_FAILED, "dot product shape mismatch: lhs " + shape_debug(*al) + ", rhs " +
+                                                  shape_debug(*bl));
+        st = validate_layout(*bl, b->len);
+        if (st != HEPH_OK) return st;
+    }
+    uint64_t count = 0;
+    st = plan_full_reduction(*al, a->len, *ol, out->len, &count);
+    if (st != HEPH_OK) return st;
+    *c = Call{Kind::Map, (int)map, const_cast<heph_buffer *>(a), *al, out, *ol};
+    c->count = count;
+    c->b = map == HEPH_MAP_DOT ? b : a;
+    c->b_l = map == HEPH_MAP_DOT ? *bl : *al;
+    return HEPH_OK;
+}
+
 heph_status run(heph_device *device, const Call &c, heph_stream stream) {
     if (c.noop) return HEPH_OK;
     heph_status st = bind(device);
@@ -586,6 +619,10 @@ heph_status run(heph_device *device, const Call &c, heph_stream stream) {
         case Kind::Scan:
             return launch_scan(device, s, c.op, c.in->dtype, c.in->ptr, c.out->ptr, c.p, c.reverse,
                                c.exclusive, nullptr);
+        case Kind::Map: {
+            void *out = static_cast<char *>(c.out->ptr) + c.out_l.offset * dtype_size(c.out->dtype);
+            return launch_map_reduce(device, s, c.op, c.in->dtype, c.in->ptr, c.in_l, c.b->ptr, c.b_l, c.count, out);
+        }
     }
     return fail(HEPH_DISPATCH_FAILED, "unknown call kind");
 }
@@ -674,6 +711,29 @@ extern "C" heph_status heph_scan_seeded(heph_device *device, heph_op op, int exc
     const void *cptr = static_cast<const char *>(carry->ptr) + carry_offset * dtype_size(carry->dtype);
     return launch_scan(device, resolve_stream(device, stream), c.op, in->dtype, in->ptr, out->ptr, c.p,
                        false, c.exclusive, cptr);
+}
+
+extern "C" heph_status heph_map_reduce_full(heph_device *device, heph_map map, const heph_buffer *a,
+                                            const heph_layout *a_layout, const heph_buffer *b,
+                                            const heph_layout *b_layout, heph_buffer *out,
+                                            const heph_layout *out_layout, heph_stream stream) {
+    Call c{};
+    heph_status st = plan_map(device, map, a, a_layout, b, b_layout, out, out_layout, &c);
+    if (st != HEPH_OK) return st;
+    return run(device, c, stream);
+}
+
+extern "C" heph_status heph_prepare_map_reduce_full(heph_device *device, heph_map map, const heph_buffer *a,
+                                                    const heph_layout *a_layout, const heph_buffer *b,
+                                                    const heph_layout *b_layout, heph_buffer *out,
+                                                    const heph_layout *out_layout, heph_prepared **out_prepared) {
+    if (!out_prepared) return fail(HEPH_INVALID_CONFIGURATION, "null output");
+    *out_prepared = nullptr;
+    Call c{};
+    heph_status st = plan_map(device, map, a, a_layout, b, b_layout, out, out_layout, &c);
+    if (st != HEPH_OK) return st;
+    *out_prepared = new heph_prepared{c};
+    return HEPH_OK;
 }
 
 extern "C" heph_status heph_prepare_reduce_full(heph_device *device, heph_op op, const heph_buffer *in,

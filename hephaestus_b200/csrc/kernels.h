@@ -23,6 +23,12 @@ heph_status launch_reduce_axis(Device *dev, cudaStream_t stream, int op, heph_dt
                                const void *in, const AxisProblem &p, void *out, bool mean,
                                uint32_t *indices, int64_t idx_base, int64_t idx_o);
 
+// Fused map-reduction (dot / identity / |x| / x^2 then sqrt / max |x|) of two
+// same-shape views into the single element at `out`.
+heph_status launch_map_reduce(Device *dev, cudaStream_t stream, int map, heph_dtype dtype, const void *a,
+                              const heph_layout &la, const void *b, const heph_layout &lb, uint64_t count,
+                              void *out);
+
 // Axis scan (rank 1 or 2).  `carry` (nullable, device) seeds line 0.
 heph_status launch_scan(Device *dev, cudaStream_t stream, int op, heph_dtype dtype,
                         const void *in, void *out, const AxisProblem &p, bool reverse,

@@ -355,3 +355,122 @@ def synth_inject_row_ties(device: CudaDevice, matrix: CudaBuffer, rows: int, col
 
 SYNTH_F32_UNIFORM_PM1, SYNTH_U32_LOW4, SYNTH_F32_NORMAL, SYNTH_F64_UNIT, SYNTH_I32_PM1000 = range(5)
 
+
+
+# ------------------------------------------------ fused map-reductions
+
+
+def _map_call(device, map_kind, a: StridedView, b, out: StridedView, stream=None):
+    al, ol = a.layout.native(), out.layout.native()
+    bl = b.layout.native() if b is not None else None
+    check(N.lib.heph_map_reduce_full(device.handle, map_kind, a.buffer.handle, ctypes.byref(al),
+                                     b.buffer.handle if b is not None else None,
+                                     ctypes.byref(bl) if bl is not None else None,
+                                     out.buffer.handle, ctypes.byref(ol), _stream(stream)))
+
+
+def _map_alloc(device, map_kind, a: StridedView, b=None) -> CudaBuffer:
+    out = device.alloc_uninitialized(a.buffer.dtype, 1)
+    _map_call(device, map_kind, a, b, StridedView(out, Layout.c_contiguous([1])))
+    return out
+
+
+def dot(device, a: StridedView, b: StridedView) -> CudaBuffer:
+    """Σ a[i]*b[i] into a new 1-element buffer (hephaestus-cuda linalg/norms.rs:357)."""
+    return _map_alloc(device, N.MAP_DOT, a, b)
+
+
+def trace(device, matrix: StridedView) -> CudaBuffer:
+    """Σ a[i][i] of a square rank-2 view (norms.rs:379): the diagonal view
+    (stride = row stride + column stride) reduced with the identity map."""
+    lay = matrix.layout
+    if lay.rank != 2 or lay.shape[0] != lay.shape[1]:
+        raise DispatchFailed(f"trace requires a square matrix, got shape {list(lay.shape)}")
+    diag = Layout.try_new([lay.shape[0]], [lay.strides[0] + lay.strides[1]], lay.offset)
+    return _map_alloc(device, N.MAP_SUM, StridedView(matrix.buffer, diag))
+
+
+def norm_l1(device, view: StridedView) -> CudaBuffer:
+    return _map_alloc(device, N.MAP_NORM_L1, view)
+
+
+def norm_l2(device, view: StridedView) -> CudaBuffer:
+    return _map_alloc(device, N.MAP_NORM_L2, view)
+
+
+def norm_max(device, view: StridedView) -> CudaBuffer:
+    return _map_alloc(device, N.MAP_NORM_MAX, view)
+
+
+class PreparedMap(Prepared):
+    """A prepared map-reduction that owns its 1-element output (prepare_dot /
+    prepare_norm_l2 of hephaestus-cuda application/prepared_map_reduction.rs)."""
+
+    def __init__(self, device, map_kind, a: StridedView, b=None):
+        out = device.alloc_zeroed(a.buffer.dtype, 1)
+        ov = StridedView(out, Layout.c_contiguous([1]))
+        al, ol = a.layout.native(), ov.layout.native()
+        bl = b.layout.native() if b is not None else None
+        h = ctypes.c_void_p()
+        check(N.lib.heph_prepare_map_reduce_full(device.handle, map_kind, a.buffer.handle, ctypes.byref(al),
+                                                 b.buffer.handle if b is not None else None,
+                                                 ctypes.byref(bl) if bl is not None else None,
+                                                 out.handle, ctypes.byref(ol), ctypes.byref(h)))
+        super().__init__(h.value, (a, b, ov))
+        self.device = device
+        self._out = out
+
+    def output(self) -> CudaBuffer:
+        return self._out
+
+    def dispatch(self, stream=None):
+        _dispatch(self.device, self, stream)
+
+
+def prepare_dot(device, a: StridedView, b: StridedView) -> PreparedMap:
+    return PreparedMap(device, N.MAP_DOT, a, b)
+
+
+def prepare_norm_l2(device, view: StridedView) -> PreparedMap:
+    return PreparedMap(device, N.MAP_NORM_L2, view)
+
+
+class CudaDenseVectorOps:
+    """The reduction half of ``DenseVectorOps`` (crates/hephaestus-core/src/domain/vector.rs:57-229):
+    one-shot and prepared dot / norms of whole contiguous buffers, read back to the host."""
+
+    @staticmethod
+    def _whole(buf):
+        return StridedView(buf, Layout.c_contiguous([len(buf)]))
+
+    def _read(self, device, map_kind, a, b=None):
+        out = _map_alloc(device, map_kind, self._whole(a), self._whole(b) if b is not None else None)
+        return device.download_owned(out)[0]
+
+    def dot(self, device, left: CudaBuffer, right: CudaBuffer):
+        if len(left) != len(right):
+            raise DispatchFailed(f"dot product shape mismatch: lhs [{len(left)}], rhs [{len(right)}]")
+        return self._read(device, N.MAP_DOT, left, right)
+
+    def norm_l1(self, device, vector: CudaBuffer):
+        return self._read(device, N.MAP_NORM_L1, vector)
+
+    def norm_l2(self, device, vector: CudaBuffer):
+        return self._read(device, N.MAP_NORM_L2, vector)
+
+    def norm_max(self, device, vector: CudaBuffer):
+        return self._read(device, N.MAP_NORM_MAX, vector)
+
+    def prepare_dot(self, device, left: CudaBuffer, right: CudaBuffer) -> PreparedMap:
+        return prepare_dot(device, self._whole(left), self._whole(right))
+
+    def dot_prepared(self, device, prepared: PreparedMap):
+        prepared.dispatch()
+        return device.download_owned(prepared.output())[0]
+
+    def prepare_norm_l2(self, device, vector: CudaBuffer) -> PreparedMap:
+        return prepare_norm_l2(device, self._whole(vector))
+
+    def norm_l2_prepared(self, device, prepared: PreparedMap):
+        prepared.dispatch()
+        return device.download_owned(prepared.output())[0]

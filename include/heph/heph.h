@@ -68,6 +68,18 @@ typedef enum heph_op {
     HEPH_MEAN = 4
 } heph_op;
 
+/* Map of a fused map-reduction — the MapReductionOp markers of
+ * hephaestus-cuda application/linalg/norms.rs:55-89: DotMap (lhs*rhs, sum),
+ * IdentityMap (lhs, sum; trace over a diagonal view), AbsMap (|lhs|, sum; L1),
+ * SquareMap (lhs*lhs, sum, then sqrt; L2), MaxAbsMap (|lhs|, max; max norm). */
+typedef enum heph_map {
+    HEPH_MAP_DOT = 0,
+    HEPH_MAP_SUM = 1,
+    HEPH_MAP_NORM_L1 = 2,
+    HEPH_MAP_NORM_L2 = 3,
+    HEPH_MAP_NORM_MAX = 4
+} heph_map;
+
 /* ScanDirection — crates/hephaestus-core/src/domain/scan.rs:38. */
 typedef enum heph_scan_direction {
     HEPH_FORWARD = 0,
@@ -238,6 +250,28 @@ heph_status heph_arg_reduce_axis(heph_device *device, heph_op op,
                                  heph_buffer *values, const heph_layout *values_layout,
                                  heph_buffer *indices, const heph_layout *indices_layout,
                                  heph_stream stream);
+
+/* ------------------------------------------ fused map-reductions (vector) */
+
+/* dot / trace / norm_l1 / norm_l2 / norm_max — hephaestus-cuda
+ * application/linalg/norms.rs:357-450, DenseVectorOps::dot/norm_l1/norm_l2/
+ * norm_max (crates/hephaestus-core/src/domain/vector.rs:57-229).  `a` (and
+ * `b` for HEPH_MAP_DOT, NULL otherwise) are strided views of the same shape
+ * (rank <= 4); `out` views one element of the same element type.  The map is
+ * fused into a single-launch reduction; HEPH_MAP_NORM_L2 needs f32/f64.
+ * Shape mismatch: "dot product shape mismatch: lhs [..], rhs [..]". */
+heph_status heph_map_reduce_full(heph_device *device, heph_map map,
+                                 const heph_buffer *a, const heph_layout *a_layout,
+                                 const heph_buffer *b, const heph_layout *b_layout,
+                                 heph_buffer *out, const heph_layout *out_layout,
+                                 heph_stream stream);
+/* prepare_dot / prepare_norm_l2 — hephaestus-cuda application/prepared_map_reduction.rs
+ * (any map here); dispatched with heph_dispatch_prepared, batchable. */
+heph_status heph_prepare_map_reduce_full(heph_device *device, heph_map map,
+                                         const heph_buffer *a, const heph_layout *a_layout,
+                                         const heph_buffer *b, const heph_layout *b_layout,
+                                         heph_buffer *out, const heph_layout *out_layout,
+                                         heph_prepared **out_prepared);
 
 /* -------------------------------------------------------- ScanOps seam */
 

@@ -268,6 +268,57 @@ int href_scan_axis(int dtype, int op, int reverse, int exclusive, const void *in
     }
 }
 
+/* ------------------------------------------------------ map reductions */
+
+#define DEFINE_MAP(SUF, T, UT, IS_FLOAT, IS_SIGNED)                                         \
+    static T SUF##_abs(T v) {                                                              \
+        if (IS_FLOAT) return v < (T)0 ? -v : (v == (T)0 ? (T)0 : v);                        \
+        if (IS_SIGNED) return v < (T)0 ? (T)((UT)0 - (UT)v) : v;                            \
+        return v;                                                                          \
+    }                                                                                      \
+    static void SUF##_map(int map, const T *a, const href_layout *la, const T *b,         \
+                          const href_layout *lb, T *out) {                                 \
+        uint64_t n = layout_size(la);                                                      \
+        int red = map == 4 ? HREF_MAX : HREF_SUM;                                          \
+        T acc = SUF##_identity(red);                                                       \
+        for (uint64_t i = 0; i < n; ++i) {                                                 \
+            T x = a[layout_offset_of(la, i)];                                              \
+            T m;                                                                           \
+            if (map == 0) m = SUF##_combine(HREF_PROD, x, b[layout_offset_of(lb, i)]);     \
+            else if (map == 1) m = x;                                                      \
+            else if (map == 3) m = SUF##_combine(HREF_PROD, x, x);                         \
+            else m = SUF##_abs(x);                                                         \
+            acc = SUF##_combine(red, acc, m);                                              \
+        }                                                                                  \
+        *out = acc;                                                                        \
+    }
+
+DEFINE_MAP(f32, float, float, 1, 1)
+DEFINE_MAP(f64, double, double, 1, 1)
+DEFINE_MAP(u32, uint32_t, uint32_t, 0, 0)
+DEFINE_MAP(i32, int32_t, uint32_t, 0, 1)
+DEFINE_MAP(i64, int64_t, uint64_t, 0, 1)
+
+int href_map_reduce(int dtype, int map, const void *a, const href_layout *la, const void *b,
+                    const href_layout *lb, void *out) {
+    if (map < 0 || map > 4) return -1;
+    if (map != 0) { b = a; lb = la; }
+    switch (dtype) {
+        case HREF_F32:
+            f32_map(map, a, la, b, lb, out);
+            if (map == 3) *(float *)out = sqrtf(*(float *)out);
+            return 0;
+        case HREF_F64:
+            f64_map(map, a, la, b, lb, out);
+            if (map == 3) *(double *)out = sqrt(*(double *)out);
+            return 0;
+        case HREF_U32: if (map == 3) return -1; u32_map(map, a, la, b, lb, out); return 0;
+        case HREF_I32: if (map == 3) return -1; i32_map(map, a, la, b, lb, out); return 0;
+        case HREF_I64: if (map == 3) return -1; i64_map(map, a, la, b, lb, out); return 0;
+        default: return -1;
+    }
+}
+
 /* -------------------------------------------------------------- generators */
 
 /* SplitMix64 output function (Steele, Lea & Flood, OOPSLA 2014), applied to

@@ -66,6 +66,13 @@ int href_scan_axis(int dtype, int op, int reverse, int exclusive, const void *in
                    const href_layout *in_layout, uint32_t axis, void *out,
                    const href_layout *out_layout);
 
+/* Fused map-reduction (map: 0 dot, 1 identity-sum, 2 |x| sum, 3 sqrt(sum x^2),
+ * 4 max |x|) of same-shape views a and b (b ignored unless map == 0):
+ * sequential left fold of map(a_i, b_i) from the reduce identity
+ * (hephaestus-cuda application/linalg/norms.rs:55-89, 357-450). */
+int href_map_reduce(int dtype, int map, const void *a, const href_layout *la, const void *b,
+                    const href_layout *lb, void *out);
+
 /* SplitMix64 (Steele, Lea & Flood 2014) counter stream:
  * h(seed, i) = splitmix64_mix(seed * 2^32 XOR i). */
 uint64_t href_hash(uint64_t seed, uint64_t index);

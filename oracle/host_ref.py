@@ -78,6 +78,7 @@ def lib():
         L.href_reduce_axis.argtypes = [i32, i32, vp, lp, ctypes.c_uint32, vp, lp]
         L.href_arg_reduce_axis.argtypes = [i32, i32, vp, lp, ctypes.c_uint32, vp, lp, vp, lp]
         L.href_scan_axis.argtypes = [i32, i32, i32, i32, vp, lp, ctypes.c_uint32, vp, lp]
+        L.href_map_reduce.argtypes = [i32, i32, vp, lp, vp, lp, vp]
         L.href_hash.argtypes = [u64, u64]
         L.href_hash.restype = u64
         L.href_generate.argtypes = [i32, u64, u64, u64, vp]
@@ -159,6 +160,19 @@ def scan_axis(storage, in_shape, axis, op=SUM, reverse=False, exclusive=False,
                                 ctypes.byref(il), axis, _ptr(out_storage), ctypes.byref(ol)),
            "scan_axis")
     return out_storage
+
+
+MAP_DOT, MAP_SUM, MAP_NORM_L1, MAP_NORM_L2, MAP_NORM_MAX = range(5)
+
+
+def map_reduce(map_kind, a, shape, strides=None, offset=0, b=None, b_strides=None, b_offset=0):
+    dt = dtype_code(a.dtype)
+    la = layout(shape, strides, offset)
+    lb = layout(shape, b_strides, b_offset) if b is not None else la
+    out = np.zeros(1, dtype=a.dtype)
+    _check(lib().href_map_reduce(dt, map_kind, _ptr(a), ctypes.byref(la), _ptr(b if b is not None else a),
+                                 ctypes.byref(lb), _ptr(out)), "map_reduce")
+    return out[0]
 
 
 # -------------------------------------------------------------- generators

@@ -207,6 +207,44 @@ for r in range(2):
 add(id="contract_scan_long_line_i32", source=f"{CONTRACT}:1913-1949", kind="scan", dtype="i32",
     input=long_in, layout=cc([2, cols]), axis=1, op="sum", reverse=False, expected=long_exp)
 
+# ------------------------------------------------------- map reductions
+MAPS = {"dot": 0, "trace": 1, "norm_l1": 2, "norm_l2": 3, "norm_max": 4}
+add(id="contract_dot", source=f"{CONTRACT}:895-927", kind="map", map="dot", dtype="f32",
+    input=[1.0, 2.0, 3.0, 4.0], layout=cc([4]), input_b=[5.0, 6.0, 7.0, 8.0], layout_b=cc([4]),
+    expected=[70.0])
+add(id="contract_trace", source=f"{CONTRACT}:929-953", kind="map", map="trace", dtype="f32",
+    input=[float(v) for v in range(1, 10)], layout=lay([3], [4]), expected=[15.0])
+add(id="contract_prepared_dot_rebind", source=f"{CONTRACT}:955-985", kind="map", map="dot", dtype="f32",
+    input=[2.0, 2.0, 2.0, 2.0], layout=cc([4]), input_b=[5.0, 6.0, 7.0, 8.0], layout_b=cc([4]),
+    expected=[52.0])
+add(id="contract_prepared_dot_reversed", source=f"{CONTRACT}:988-1003", kind="map", map="dot", dtype="f32",
+    input=[2.0, 2.0, 2.0, 2.0], layout=lay([4], [-1], 3), input_b=[5.0, 6.0, 7.0, 8.0], layout_b=cc([4]),
+    expected=[52.0])
+add(id="contract_norm_l2_transposed", source=f"{CONTRACT}:1005-1022", kind="map", map="norm_l2", dtype="f32",
+    input=[1.0, 2.0, 3.0, 4.0], layout=lay([2, 2], [1, 2]), expected=[math.sqrt(30.0)],
+    tolerance=2 * 1.1920929e-07 * math.sqrt(30.0))
+add(id="contract_norm_l2_rewrite", source=f"{CONTRACT}:1023-1029", kind="map", map="norm_l2", dtype="f32",
+    input=[4.0] * 4, layout=lay([2, 2], [1, 2]), expected=[8.0])
+add(id="contract_empty_dot", source=f"{CONTRACT}:1034-1048", kind="map", map="dot", dtype="f32", input=[],
+    layout=cc([0]), input_b=[], layout_b=cc([0]), expected=[0.0])
+add(id="contract_empty_norm_l2", source=f"{CONTRACT}:1050-1060", kind="map", map="norm_l2", dtype="f32",
+    input=[], layout=cc([0]), expected=[0.0])
+add(id="contract_dot_shape_mismatch", source=f"{CONTRACT}:1062-1077", kind="map", map="dot", dtype="f32",
+    input=[1.0, 2.0, 3.0, 4.0], layout=cc([4]), input_b=[5.0, 6.0, 7.0, 8.0], layout_b=cc([3]),
+    error_prefix="dot product shape mismatch:")
+add(id="contract_norm_layout_rejected", source=f"{CONTRACT}:1079-1090", kind="map", map="norm_l2", dtype="f32",
+    input=[1.0, 2.0, 3.0, 4.0], layout=lay([3], [1], 2), error_prefix="layout rejected:")
+for m, exp, line in [("norm_l1", 10.0, "1094-1111"), ("norm_l2", math.sqrt(30.0), "1112-1118"),
+                     ("norm_max", 4.0, "1119-1124")]:
+    add(id=f"contract_{m}", source=f"{CONTRACT}:{line}", kind="map", map=m, dtype="f32",
+        input=[-1.0, 2.0, -3.0, 4.0], layout=cc([4]), expected=[exp],
+        **({"tolerance": 1e-5} if m == "norm_l2" else {}))
+add(id="contract_dot_reversed_values", source=f"{CONTRACT}:1128-1154", kind="map", map="dot", dtype="f32",
+    input=[-1.0, 2.0, -3.0, 4.0], layout=lay([4], [-1], 3), input_b=[1.0, 2.0, 3.0, 4.0], layout_b=cc([4]),
+    expected=[0.0])
+add(id="contract_norm_l1_reversed", source=f"{CONTRACT}:1155-1156", kind="map", map="norm_l1", dtype="f32",
+    input=[-1.0, 2.0, -3.0, 4.0], layout=lay([4], [-1], 3), expected=[10.0])
+
 # ---------------------------------------------------------------- widths
 add(id="contract_width_192", source=f"{CONTRACT}:670-690", kind="width", width=192,
     error="reduction block width 192 must be a power of two")

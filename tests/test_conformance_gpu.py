@@ -195,3 +195,50 @@ def test_prepared_batch_submission(device):
     from hephaestus_b200 import InvalidConfiguration
     with pytest.raises(InvalidConfiguration):
         S.Batch(device, [pscan])
+
+
+MAPS = {"dot": 0, "trace": 1, "norm_l1": 2, "norm_l2": 3, "norm_max": 4}
+
+
+@pytest.mark.parametrize("cid", cases_of_kind("map"))
+def test_map_reduction_clause(device, cid):
+    from hephaestus_b200 import _native as N
+    import ctypes
+    from hephaestus_b200.core import check
+    c = CASES[cid]
+    a, _ = upload_input(device, c)
+    b = None
+    if "input_b" in c:
+        b, _ = upload_input(device, dict(c, input=c["input_b"]))
+    out = device.upload(np.array([9.0], np.float32))
+    ol = Layout.c_contiguous([1])
+    av = StridedView(a, L(c["layout"]))
+    bv = StridedView(b, L(c["layout_b"])) if b is not None else None
+    if "error_prefix" in c:
+        with pytest.raises(DispatchFailed) as e:
+            S._map_call(device, MAPS[c["map"]], av, bv, StridedView(out, ol))
+        assert e.value.message.startswith(c["error_prefix"]), c["source"]
+        assert device.download_owned(out)[0] == 9.0
+        return
+    S._map_call(device, MAPS[c["map"]], av, bv, StridedView(out, ol))
+    got = float(device.download_owned(out)[0])
+    assert abs(got - c["expected"][0]) <= c.get("tolerance", 0.0), (c["source"], got)
+
+
+def test_dense_vector_ops_prepared(device):
+    """contract.rs:955-1029: prepared dot / norm_l2 reuse their output and observe rewrites."""
+    ops = S.CudaDenseVectorOps()
+    lhs = device.upload(np.array([1, 2, 3, 4], np.float32))
+    rhs = device.upload(np.array([5, 6, 7, 8], np.float32))
+    pd = ops.prepare_dot(device, lhs, rhs)
+    out_ptr = pd.output().device_ptr()
+    assert ops.dot_prepared(device, pd) == 70.0
+    device.write_buffer(lhs, np.full(4, 2, np.float32))
+    assert ops.dot_prepared(device, pd) == 52.0 and pd.output().device_ptr() == out_ptr
+    pn = ops.prepare_norm_l2(device, lhs)
+    assert ops.norm_l2_prepared(device, pn) == 4.0
+    assert ops.norm_l1(device, rhs) == 26.0 and ops.norm_max(device, rhs) == 8.0
+    t = S.trace(device, StridedView(device.upload(np.arange(1, 10, dtype=np.float32)), Layout.c_contiguous([3, 3])))
+    assert device.download_owned(t)[0] == 15.0
+    with pytest.raises(DispatchFailed):
+        S.trace(device, StridedView(lhs, Layout.c_contiguous([1, 4])))

@@ -146,3 +146,20 @@ def test_mt_baselines_agree_with_sequential(oracle):
     c = oracle.generate(oracle.GEN_F64_UNIT, 3, 50 * 300)
     np.testing.assert_allclose(oracle.col_sum_f64_mt(c, 50, 300, 2),
                                oracle.reduce_axis(c, [50, 300], 0).ravel(), rtol=1e-12)
+
+
+MAPS = {"dot": 0, "trace": 1, "norm_l1": 2, "norm_l2": 3, "norm_max": 4}
+
+
+@pytest.mark.parametrize("case_id", cases_of_kind("map"))
+def test_map_reduction_fixture(oracle, golden, case_id):
+    c = golden[case_id]
+    a = input_array(c)
+    lay = c["layout"]
+    if "error_prefix" in c:
+        return  # planner behaviour, checked on the GPU path
+    b = np.array(c["input_b"], dtype=a.dtype) if "input_b" in c else None
+    lb = c.get("layout_b", lay)
+    got = oracle.map_reduce(MAPS[c["map"]], a, lay["shape"], lay["strides"], lay["offset"], b=b,
+                            b_strides=lb["strides"], b_offset=lb["offset"])
+    assert abs(float(got) - c["expected"][0]) <= c.get("tolerance", 0.0), c["source"]

@@ -360,3 +360,33 @@ def test_scan_host_pipeline(device, oracle, dt, exc):
             np.testing.assert_allclose(y.astype(np.float64), want.astype(np.float64), rtol=0, atol=tol(dt, x))
         else:
             np.testing.assert_array_equal(y, want, err_msg=f"n={n} chunk={chunk}")
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+@pytest.mark.parametrize("map_kind", [0, 1, 2, 3, 4])
+def test_map_reduction_parity(device, oracle, dt, map_kind):
+    import hephaestus_b200.seams as S
+    if map_kind == 3 and np.dtype(dt).kind != "f":
+        pytest.skip("norm_l2 is defined for floating-point types")
+    rng = np.random.default_rng(40 + map_kind)
+    for n in [0, 1, 33, 4097, 1_000_003]:
+        x, y = rand(dt, n, rng), rand(dt, n, rng)
+        xb = device.upload(x) if n else device.alloc_zeroed(dt, 0)
+        yb = device.upload(y) if n else device.alloc_zeroed(dt, 0)
+        out = device.alloc_zeroed(dt, 1)
+        views = [(Layout.c_contiguous([n]), Layout.c_contiguous([n]))]
+        if n > 8:
+            views.append((Layout.try_new([n // 2], [2], 1), Layout.try_new([n // 2], [-2], n - 1)))
+        for la, lb in views:
+            S._map_call(device, map_kind, StridedView(xb, la), StridedView(yb, lb) if map_kind == 0 else None,
+                        StridedView(out, Layout.c_contiguous([1])))
+            want = oracle.map_reduce(map_kind, x, la.shape, la.strides, la.offset,
+                                     b=y if map_kind == 0 else None, b_strides=lb.strides, b_offset=lb.offset)
+            got = device.download_owned(out)[0]
+            if np.dtype(dt).kind == "f":
+                scale = float(np.abs(x.astype(np.float64) * (np.abs(y) if map_kind == 0 else 1)).sum()) \
+                    if map_kind != 3 else float(np.sqrt((x.astype(np.float64) ** 2).sum()))
+                t = {np.dtype(np.float32): 1e-5, np.dtype(np.float64): 1e-12}[np.dtype(dt)] * max(scale, 1.0)
+                assert abs(float(got) - float(want)) <= t, (n, la, got, want)
+            else:
+                assert got == want, (n, la)
