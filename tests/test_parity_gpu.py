@@ -380,8 +380,11 @@ def test_map_reduction_parity(device, oracle, dt, map_kind):
         for la, lb in views:
             S._map_call(device, map_kind, StridedView(xb, la), StridedView(yb, lb) if map_kind == 0 else None,
                         StridedView(out, Layout.c_contiguous([1])))
-            want = oracle.map_reduce(map_kind, x, la.shape, la.strides, la.offset,
-                                     b=y if map_kind == 0 else None, b_strides=lb.strides, b_offset=lb.offset)
+            # Floats: the oracle's fold in f64 (a sequential f32 fold of 10^6
+            # positive terms is itself off by ~1e-5 relative).
+            xr, yr = (x.astype(np.float64), y.astype(np.float64)) if np.dtype(dt).kind == "f" else (x, y)
+            want = oracle.map_reduce(map_kind, xr, la.shape, la.strides, la.offset,
+                                     b=yr if map_kind == 0 else None, b_strides=lb.strides, b_offset=lb.offset)
             got = device.download_owned(out)[0]
             if np.dtype(dt).kind == "f":
                 scale = float(np.abs(x.astype(np.float64) * (np.abs(y) if map_kind == 0 else 1)).sum()) \
