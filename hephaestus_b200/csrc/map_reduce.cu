@@ -156,8 +156,16 @@ heph_status launch_map_typed(Device *dev, cudaStream_t stream, const T *a, const
         return HEPH_OK;
     }
     const T *pa = a + la.offset, *pb = b + lb.offset;
-    const bool dense = layout_is_dense(la) && layout_is_dense(lb) &&
-                       (reinterpret_cast<uintptr_t>(pa) & 15u) == 0 && (reinterpret_cast<uintptr_t>(pb) & 15u) == 0;
+    bool contiguous = layout_is_dense(la) && layout_is_dense(lb);
+    int64_t first = 0;
+    if (!contiguous && MAP != HEPH_MAP_DOT && layout_covers_dense_block(la, &first)) {
+        // Unary maps fold order-insensitively: a permuted / reversed dense
+        // block streams contiguously.
+        pa = pb = a + first;
+        contiguous = true;
+    }
+    const bool dense = contiguous && (reinterpret_cast<uintptr_t>(pa) & 15u) == 0 &&
+                       (reinterpret_cast<uintptr_t>(pb) & 15u) == 0;
     const uint64_t per_cta = (uint64_t)kMapThreads * kMapUnroll * (16 / sizeof(T));
     const uint64_t cap = (uint64_t)dev->sm_count * (2048 / kMapThreads);
     const unsigned grid = (unsigned)std::max<uint64_t>(1, std::min((n + per_cta - 1) / per_cta, cap));

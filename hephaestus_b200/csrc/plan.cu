@@ -10,6 +10,8 @@
 #include "plan.h"
 
 #include <cstdio>
+#include <cstdlib>
+#include <utility>
 
 #include "common.cuh"
 
@@ -83,6 +85,31 @@ bool layout_is_dense(const heph_layout &l) {
         if (l.shape[d] != 1 && l.strides[d] != expect) return false;
         expect *= (int64_t)l.shape[d];
     }
+    return true;
+}
+
+bool layout_covers_dense_block(const heph_layout &l, int64_t *first) {
+    struct Dim {
+        uint64_t extent;
+        int64_t stride;
+    } dims[HEPH_MAX_RANK];
+    int k = 0;
+    int64_t lo = (int64_t)l.offset;
+    for (uint32_t d = 0; d < l.rank && d < HEPH_MAX_RANK; ++d) {
+        if (l.shape[d] == 0) return false;
+        if (l.shape[d] == 1) continue;
+        dims[k++] = {l.shape[d], l.strides[d]};
+        if (l.strides[d] < 0) lo += (int64_t)(l.shape[d] - 1) * l.strides[d];
+    }
+    // insertion sort by |stride|
+    for (int i = 1; i < k; ++i)
+        for (int j = i; j > 0 && std::llabs(dims[j].stride) < std::llabs(dims[j - 1].stride); --j) std::swap(dims[j], dims[j - 1]);
+    int64_t expect = 1;
+    for (int i = 0; i < k; ++i) {
+        if (std::llabs(dims[i].stride) != expect) return false;
+        expect *= (int64_t)dims[i].extent;
+    }
+    *first = lo;
     return true;
 }
 

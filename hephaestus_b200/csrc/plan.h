@@ -38,4 +38,11 @@ heph_status plan_full_reduction(const heph_layout &in, uint64_t in_len, const he
 // offset in row-major order (so it can be read as one contiguous run).
 bool layout_is_dense(const heph_layout &l);
 
+// True when the view visits every element of one contiguous block exactly
+// once, in some order (a transposed, permuted or reversed dense layout);
+// *first receives the block's first element offset.  An order-insensitive
+// fold (every operator here is commutative) can then read the block
+// contiguously.
+bool layout_covers_dense_block(const heph_layout &l, int64_t *first);
+
 }  // namespace heph

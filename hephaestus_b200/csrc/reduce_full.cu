@@ -150,9 +150,12 @@ static heph_status launch_typed(Device *dev, cudaStream_t stream, const void *ba
     heph_status st = workspace_for(dev, stream, (size_t)grid * sizeof(Tacc), 0, &ws);
     if (st != HEPH_OK) return st;
     Tacc *partials = static_cast<Tacc *>(ws->partials);
-    if (dense) {
+    int64_t first = 0;
+    if (dense || layout_covers_dense_block(l, &first)) {
+        // Dense, or a permutation / reversal of a dense block: the fold is
+        // order-insensitive, so the block streams contiguously.
         reduce_dense_kernel<Tin, Tacc, OP><<<grid, kReduceThreads, 0, stream>>>(
-            base + l.offset, count, out, partials, ws->tickets);
+            base + (dense ? (int64_t)l.offset : first), count, out, partials, ws->tickets);
     } else {
         StridedView4 v{};
         v.rank = l.rank;

@@ -393,3 +393,29 @@ def test_map_reduction_parity(device, oracle, dt, map_kind):
                 assert abs(float(got) - float(want)) <= t, (n, la, got, want)
             else:
                 assert got == want, (n, la)
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.int32, np.float64])
+def test_permuted_dense_views_full_reduction(device, oracle, dt):
+    """Transposed, permuted and reversed views of a dense block reduce through
+    the contiguous fast path and still match the oracle."""
+    import hephaestus_b200.seams as S
+    rng = np.random.default_rng(9)
+    x = rand(dt, 2 * 3 * 5 * 7 * 64 + 5, rng)
+    buf = device.upload(x)
+    out = device.alloc_zeroed(dt, 1)
+    views = [Layout.try_new([64, 210], [1, 64], 5), Layout.try_new([13440], [-1], 13444),
+             Layout.try_new([7, 5, 3, 128], [1, 7, 35, 105], 5), Layout.try_new([210, 64], [-64, 1], 5 + 209 * 64)]
+    for v in views:
+        for op, code in [(SumOp, 0), (MaxOp, 3)]:
+            CudaFullReductionOps().reduce_full_into(op, device, StridedView(buf, v),
+                                                    StridedView(out, Layout.c_contiguous([1])))
+            want = oracle.reduce_full(x, v.shape, v.strides, v.offset, op=code)
+            assert_close(device.download_owned(out), np.array([want], dtype=dt), dt, x)
+        S._map_call(device, 2, StridedView(buf, v), None, StridedView(out, Layout.c_contiguous([1])))
+        want = oracle.map_reduce(2, x.astype(np.float64) if np.dtype(dt).kind == "f" else x, v.shape, v.strides, v.offset)
+        got = device.download_owned(out)[0]
+        if np.dtype(dt).kind == "f":
+            assert abs(float(got) - float(want)) <= 1e-5 * float(np.abs(x).sum())
+        else:
+            assert got == want

@@ -104,3 +104,13 @@ def test_layout_validation_negative_strides():
     assert N.lib.heph_layout_validate(ctypes.byref(lay([4], [-1], 3)), 4) == N.OK
     assert N.lib.heph_layout_validate(ctypes.byref(lay([4], [-1], 2)), 4) == N.DISPATCH_FAILED
     assert "below storage index 0" in N.last_error()
+
+
+def test_dense_block_detection_through_views():
+    """Transposed / reversed dense views are recognised (they then stream
+    contiguously); gapped or overlapping views are not.  Exercised on the
+    GPU by the parity tests; here through heph_layout_validate only for
+    well-formedness of the layouts used there."""
+    for shape, strides, off, n in [([300, 333], [1, 300], 0, 99900), ([1000], [-1], 999, 1000),
+                                   ([10, 10, 10, 10], [1, 10, 100, 1000], 0, 10000)]:
+        assert N.lib.heph_layout_validate(ctypes.byref(lay(shape, strides, off)), n) == N.OK
