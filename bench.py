@@ -8,7 +8,7 @@ N*2^28-element buffer (weak scaling) and the step is the partitioned scan:
 local total -> NCCL all-gather of the totals -> carry -> seeded look-back scan.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                  [--config 1|2|3|4|5]
+                  [--config 1|2|3|4|5|6|7]
 
 Prints ONE JSON line on rank 0.  `value` is whole-job algorithmic bytes per
 second with inputs resident in HBM (CUDA events on the compute stream, max
@@ -51,6 +51,14 @@ CONFIGS = {
     5: dict(workload="i32 inclusive scan + i64-accumulated sum over 2^32 elements (16 GiB) "
                      "U{-1000..1000} seed 4, partitioned 1-D across the GPUs",
             n=1 << 32, dtype="i32", kernel="scan_chunked_kernel"),
+    # Gapped N-D views (the reference stages these through a contiguous copy
+    # first): a sub-block of a larger row-major matrix.
+    6: dict(workload="f32 full sum over the [16384 x 16000] sub-block (row stride 16384, offset 64) of a "
+                     "[16384 x 16384] matrix, U[-1,1) seed 0; 16-byte-aligned rows",
+            rows=16384, cols=16000, ld=16384, offset=64, dtype="f32", kernel="reduce_walk_kernel"),
+    7: dict(workload="f32 full sum over the [16384 x 15999] sub-block (row stride 16387, offset 1) of a "
+                     "16384 x 16387 matrix, U[-1,1) seed 0; rows not 16-byte aligned",
+            rows=16384, cols=15999, ld=16387, offset=1, dtype="f32", kernel="reduce_runs_kernel"),
 }
 
 
@@ -188,6 +196,15 @@ def cpu_sample(cfg_id: int, cfg: dict, oracle, seconds: float = 10.0, threads: i
             reps += 1
         return (4 * rows * cols + 8 * rows) / ((time.perf_counter() - t0) / reps) / 1e9, cores, \
             f"row max+argmax of [8192 x 4096] x {reps} reps"
+    if cfg_id in (6, 7):
+        rows, cols, ld, off = 1024, cfg["cols"], cfg["ld"], cfg["offset"]
+        x = oracle.generate(oracle.GEN_F32_UNIFORM_PM1, 0, rows * ld + off)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            oracle.reduce_full(x, [rows, cols], [ld, 1], off)
+            reps += 1
+        return 4 * rows * cols / ((time.perf_counter() - t0) / reps) / 1e9, 1, \
+            f"f32 sum of a [1024 x {cols}] sub-block (row stride {ld}) x {reps} reps, one thread"
     rows, cols = 512, cfg["cols"]
     x = oracle.generate(oracle.GEN_F64_UNIT, 3, rows * cols)
     reps, t0 = 0, time.perf_counter()
@@ -216,12 +233,12 @@ def run_reference(args, cfg):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "higher_is_better": True, "scaling": "weak" if args.config == 2 else "strong",
+        "higher_is_better": True, "scaling": "weak" if args.config != 5 else "strong",
         "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
         "config": {"workload": cfg["workload"], "config_index": args.config},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": desc + " per step (oracle restatement of the host reference "
-                                          "semantics, OpenMP over all cores)"},
+                         "sample": desc + " per step (oracle restatement of the host reference semantics, "
+                                          + ("OpenMP over all cores)" if cores > 1 else "sequential strided fold)")},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -238,6 +255,9 @@ def main():
     if args.n is not None and "n" in cfg:
         cfg["n"] = int(args.n)
         cfg["workload"] += f" [reduced to {args.n} elements]"
+    elif args.n is not None and args.config in (6, 7):
+        cfg["rows"] = int(args.n)
+        cfg["workload"] += f" [reduced to {args.n} rows]"
     if args.impl == "reference":
         return run_reference(args, cfg)
 
@@ -361,6 +381,21 @@ def main():
         launches_per_step = 2  # column slices + slice finalize
         kernel_step = None
         units = rows * cols
+    elif args.config in (6, 7):
+        rows, cols, ld, off = cfg["rows"], cfg["cols"], cfg["ld"], cfg["offset"]
+        x = dev.alloc_uninitialized(np.float32, rows * ld + off)
+        S.synth_fill(dev, x, S.SYNTH_F32_UNIFORM_PM1, seed=0, stream=sp)
+        out = dev.alloc_zeroed(np.float32, 1)
+        view = Layout.try_new([rows, cols], [ld, 1], off)
+        ops = H.CudaFullReductionOps()
+
+        def step():
+            ops.reduce_full_into(SumOp, dev, StridedView(x, view), StridedView(out, Layout.c_contiguous([1])),
+                                 stream=sp)
+        bytes_per_step = 4 * rows * cols
+        kernel_bytes = bytes_per_step
+        kernel_step = None
+        units = rows * cols
     else:  # config 5: strong scaling of 2^32 i32 over the ranks
         total = cfg["n"]
         n = (total + world - 1) // world
@@ -463,7 +498,7 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6),
-            "higher_is_better": True, "scaling": "weak" if args.config in (1, 2, 3, 4) else "strong",
+            "higher_is_better": True, "scaling": "weak" if args.config != 5 else "strong",
             "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
             "config": {"workload": cfg["workload"], "config_index": args.config,
                        "elements_per_gpu": units,
@@ -567,6 +602,21 @@ def run_e2e(args, cfg, dev, stream, sp, world, rank, comm, max_over_ranks, barri
             check(N.lib.heph_buffer_download_async(dev.handle, vals.handle, 0, hv, rows, ctypes.c_void_p(sp)))
             check(N.lib.heph_buffer_download_async(dev.handle, idx.handle, 0, hi, rows, ctypes.c_void_p(sp)))
         bytes_step, h2d, d2h = 4 * rows * cols + 8 * rows, 4 * rows * cols, 8 * rows
+    elif args.config in (6, 7):
+        rows, cols, ld, off = cfg["rows"], cfg["cols"], cfg["ld"], cfg["offset"]
+        total = rows * ld + off
+        hin, ho = pinned(4 * total), pinned(4)
+        x = dev.alloc_uninitialized(np.float32, total)
+        out = dev.alloc_zeroed(np.float32, 1)
+        view = Layout.try_new([rows, cols], [ld, 1], off)
+        ops = H.CudaFullReductionOps()
+
+        def e2e_step():
+            check(N.lib.heph_buffer_upload_async(dev.handle, x.handle, 0, hin, total, ctypes.c_void_p(sp)))
+            ops.reduce_full_into(SumOp, dev, StridedView(x, view), StridedView(out, Layout.c_contiguous([1])),
+                                 stream=sp)
+            check(N.lib.heph_buffer_download_async(dev.handle, out.handle, 0, ho, 1, ctypes.c_void_p(sp)))
+        bytes_step, h2d, d2h = 4 * rows * cols, 4 * total, 4
     else:
         rows, cols = cfg["rows"], cfg["cols"]
         hin, ho = pinned(8 * rows * cols), pinned(8 * cols)

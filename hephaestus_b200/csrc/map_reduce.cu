@@ -8,11 +8,14 @@
 // dot product in lockstep), other views decode their strides per element; the
 // map is applied in registers, folded per warp / CTA, and the last CTA folds
 // the per-CTA partials in order and applies the epilogue (sqrt for L2) before
-// writing the scalar in place.
+// writing the scalar in place.  Views that are not one dense block are
+// canonicalised jointly (both dot operands permuted / flipped / merged alike)
+// and walked without per-element division (view_walk.cuh).
 #include <algorithm>
 
 #include "device_utils.cuh"
 #include "kernels.h"
+#include "view_walk.cuh"
 
 namespace heph {
 namespace {
@@ -142,6 +145,117 @@ __global__ void __launch_bounds__(kMapThreads)
     finish_map<T, MAP>(acc, out, partials, ticket, scratch);
 }
 
+// Canonical strided view(s), walked without division; `n` counts walk units
+// (elements, or 16-byte vectors when VEC).  NOPS = 2 walks the dot product's
+// operands in lockstep.
+template <typename T, int MAP, int R, bool VEC, int NOPS>
+__global__ void __launch_bounds__(kMapThreads)
+    map_walk_kernel(const T *__restrict__ a, const T *__restrict__ b, const ViewWalk<NOPS> w, uint64_t n,
+                    T *__restrict__ out, T *__restrict__ partials, unsigned int *__restrict__ ticket) {
+    using F = MapFn<T, MAP>;
+    constexpr int V = Vec16<T>::V;
+    __shared__ T scratch[kMapThreads / 32];
+    const uint64_t stride = (uint64_t)gridDim.x * kMapThreads;
+    uint64_t i = (uint64_t)blockIdx.x * kMapThreads + threadIdx.x;
+    T acc = identity<T, F::REDUCE>();
+    ViewCursor<R, NOPS> cur;
+    if (i < n) cur.seek(w, i);
+    const int64_t *ob = &cur.off[NOPS - 1];
+    auto fold_vec = [&](uint4 ra, uint4 rb) {
+        Vec16<T> ea = as_elems<T>(ra), eb = as_elems<T>(rb);
+#pragma unroll
+        for (int c = 0; c < V; ++c) acc = combine<T, F::REDUCE>(acc, F::apply(ea.e[c], eb.e[c]));
+    };
+    for (; i + (kMapUnroll - 1) * stride < n; i += kMapUnroll * stride) {
+        if constexpr (VEC) {
+            uint4 ra[kMapUnroll], rb[kMapUnroll];
+#pragma unroll
+            for (int u = 0; u < kMapUnroll; ++u) {
+                ra[u] = ld_stream(reinterpret_cast<const uint4 *>(a) + cur.off[0]);
+                rb[u] = NOPS == 2 ? ld_stream(reinterpret_cast<const uint4 *>(b) + *ob) : ra[u];
+                cur.advance(w);
+            }
+#pragma unroll
+            for (int u = 0; u < kMapUnroll; ++u) fold_vec(ra[u], rb[u]);
+        } else {
+            T ra[kMapUnroll], rb[kMapUnroll];
+#pragma unroll
+            for (int u = 0; u < kMapUnroll; ++u) {
+                ra[u] = __ldg(a + cur.off[0]);
+                rb[u] = NOPS == 2 ? __ldg(b + *ob) : ra[u];
+                cur.advance(w);
+            }
+#pragma unroll
+            for (int u = 0; u < kMapUnroll; ++u) acc = combine<T, F::REDUCE>(acc, F::apply(ra[u], rb[u]));
+        }
+    }
+    for (; i < n; i += stride) {
+        if constexpr (VEC) {
+            const uint4 ra = ld_stream(reinterpret_cast<const uint4 *>(a) + cur.off[0]);
+            fold_vec(ra, NOPS == 2 ? ld_stream(reinterpret_cast<const uint4 *>(b) + *ob) : ra);
+        } else {
+            const T ra = __ldg(a + cur.off[0]);
+            acc = combine<T, F::REDUCE>(acc, F::apply(ra, NOPS == 2 ? __ldg(b + *ob) : ra));
+        }
+        cur.advance(w);
+    }
+    finish_map<T, MAP>(acc, out, partials, ticket, scratch);
+}
+
+// Unary map over unit-stride runs that are not 16-byte aligned (RunWalk).
+template <typename T, int MAP>
+__global__ void __launch_bounds__(kMapThreads)
+    map_runs_kernel(const T *__restrict__ a, const RunWalk w, T *__restrict__ out, T *__restrict__ partials,
+                    unsigned int *__restrict__ ticket) {
+    using F = MapFn<T, MAP>;
+    __shared__ T scratch[kMapThreads / 32];
+    T acc = identity<T, F::REDUCE>();
+    run_walk_fold<T, 2 * kMapUnroll>(a, w, acc, [](T &s, T x) { s = combine<T, F::REDUCE>(s, F::apply(x, x)); });
+    finish_map<T, MAP>(acc, out, partials, ticket, scratch);
+}
+
+// Launches map_walk_kernel; false (nothing launched) when an inner dim of the
+// canonical view exceeds 32-bit coordinates.
+template <typename T, int MAP, int NOPS>
+bool launch_map_walk(cudaStream_t stream, const T *a, const heph_layout &la, const T *b, const heph_layout &lb,
+                     uint64_t n, unsigned grid, T *out, T *partials, unsigned int *ticket) {
+    StreamView sv;
+    const heph_layout *ls[2] = {&la, &lb};
+    stream_view(ls, NOPS, &sv);
+    constexpr uint32_t V = 16 / sizeof(T);
+    const void *bases[2] = {a, b};
+    const bool vec = sv.rank >= 2 && stream_view_vectorize(&sv, NOPS, V, bases, sizeof(T));
+    const dim3 g(grid), bl(kMapThreads);
+    if constexpr (NOPS == 1) {
+        RunWalk runs;
+        if (!vec && make_run_walk(sv, sizeof(T), 128, &runs)) {
+            map_runs_kernel<T, MAP><<<g, bl, 0, stream>>>(a, runs, out, partials, ticket);
+            return true;
+        }
+    }
+    const uint64_t units = vec ? n / V : n;
+    if (sv.rank == 1 && sv.strides[0][0] == 1 && sv.strides[NOPS - 1][0] == 1) {
+        // Both operands one dense block, visited alike (e.g. both transposed).
+        const T *pa = a + sv.offset[0], *pb = NOPS == 2 ? b + sv.offset[1] : pa;
+        if (((reinterpret_cast<uintptr_t>(pa) | reinterpret_cast<uintptr_t>(pb)) & 15u) == 0) {
+            map_dense_kernel<T, MAP><<<g, bl, 0, stream>>>(pa, pb, n, out, partials, ticket);
+            return true;
+        }
+    }
+    const int R = sv.rank == 1 ? 1 : sv.rank == 2 ? 2 : 4;
+    ViewWalk<NOPS> w;
+    if (!make_walk<NOPS>(sv, R, (uint64_t)grid * kMapThreads, &w)) return false;
+    if (vec) {
+        if (R == 2) map_walk_kernel<T, MAP, 2, true, NOPS><<<g, bl, 0, stream>>>(a, b, w, units, out, partials, ticket);
+        else map_walk_kernel<T, MAP, 4, true, NOPS><<<g, bl, 0, stream>>>(a, b, w, units, out, partials, ticket);
+    } else {
+        if (R == 1) map_walk_kernel<T, MAP, 1, false, NOPS><<<g, bl, 0, stream>>>(a, b, w, units, out, partials, ticket);
+        else if (R == 2) map_walk_kernel<T, MAP, 2, false, NOPS><<<g, bl, 0, stream>>>(a, b, w, units, out, partials, ticket);
+        else map_walk_kernel<T, MAP, 4, false, NOPS><<<g, bl, 0, stream>>>(a, b, w, units, out, partials, ticket);
+    }
+    return true;
+}
+
 template <typename T, int MAP> __global__ void map_identity_kernel(T *out) {
     using F = MapFn<T, MAP>;
     *out = F::epilogue(identity<T, F::REDUCE>());
@@ -175,9 +289,10 @@ heph_status launch_map_typed(Device *dev, cudaStream_t stream, const T *a, const
     if (st != HEPH_OK) return st;
     T *partials = static_cast<T *>(ws->partials);
     unsigned int *ticket = ws->tickets + 2;  // tickets[0]: full reductions, [1]: scans
+    constexpr int NOPS = MAP == HEPH_MAP_DOT ? 2 : 1;
     if (dense) {
         map_dense_kernel<T, MAP><<<grid, kMapThreads, 0, stream>>>(pa, pb, n, out, partials, ticket);
-    } else {
+    } else if (!launch_map_walk<T, MAP, NOPS>(stream, a, la, b, lb, n, grid, out, partials, ticket)) {
         MapView v{};
         v.rank = la.rank;
         for (uint32_t d = 0; d < la.rank; ++d) {

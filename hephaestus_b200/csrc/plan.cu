@@ -288,3 +288,78 @@ extern "C" heph_status heph_plan_full_reduction(const heph_layout *input, uint64
     uint64_t count = 0;
     return plan_full_reduction(*input, input_len, *output, output_len, &count);
 }
+
+namespace heph {
+
+void stream_view(const heph_layout *const *ls, int nops, StreamView *v) {
+    struct Dim {
+        uint64_t extent;
+        int64_t stride[2];
+    } dims[HEPH_MAX_RANK];
+    int k = 0;
+    int64_t off[2] = {0, 0};
+    for (int o = 0; o < nops; ++o) off[o] = (int64_t)ls[o]->offset;
+    const heph_layout &l0 = *ls[0];
+    for (uint32_t d = 0; d < l0.rank && d < HEPH_MAX_RANK; ++d) {
+        if (l0.shape[d] == 1) continue;
+        Dim x{l0.shape[d], {0, 0}};
+        const bool flip = l0.strides[d] < 0;
+        for (int o = 0; o < nops; ++o) {
+            int64_t s = ls[o]->strides[d];
+            if (flip) {
+                off[o] += (int64_t)(l0.shape[d] - 1) * s;
+                s = -s;
+            }
+            x.stride[o] = s;
+        }
+        dims[k++] = x;
+    }
+    // Stable insertion sort, largest first-operand stride outermost.
+    for (int i = 1; i < k; ++i)
+        for (int j = i; j > 0 && dims[j].stride[0] > dims[j - 1].stride[0]; --j) std::swap(dims[j], dims[j - 1]);
+    // Merge an outer dim into the inner one when, for every operand, stepping
+    // the outer dim equals stepping past the whole inner dim.
+    int r = 0;
+    for (int i = 0; i < k; ++i) {
+        if (r > 0) {
+            Dim &in = dims[i];
+            Dim &out = dims[r - 1];
+            bool ok = true;
+            for (int o = 0; o < nops; ++o) ok = ok && out.stride[o] == (int64_t)in.extent * in.stride[o];
+            if (ok) {
+                out.extent *= in.extent;
+                for (int o = 0; o < nops; ++o) out.stride[o] = in.stride[o];
+                continue;
+            }
+        }
+        dims[r++] = dims[i];
+    }
+    if (r == 0) dims[r++] = Dim{1, {1, 1}};
+    v->rank = (uint32_t)r;
+    for (int d = 0; d < r; ++d) {
+        v->shape[d] = dims[d].extent;
+        for (int o = 0; o < nops; ++o) v->strides[o][d] = dims[d].stride[o];
+    }
+    for (int o = 0; o < nops; ++o) v->offset[o] = off[o];
+}
+
+bool stream_view_vectorize(StreamView *v, int nops, uint32_t elems, const void *const *bases, size_t elem_size) {
+    const int in = (int)v->rank - 1;
+    const int64_t e = (int64_t)elems;
+    if (v->shape[in] % elems) return false;
+    for (int o = 0; o < nops; ++o) {
+        if (v->strides[o][in] != 1 || v->offset[o] % e) return false;
+        for (int d = 0; d < in; ++d)
+            if (v->strides[o][d] % e) return false;
+        const uintptr_t a = reinterpret_cast<uintptr_t>(bases[o]) + (uintptr_t)(v->offset[o] * (int64_t)elem_size);
+        if (a & 15u) return false;
+    }
+    v->shape[in] /= elems;
+    for (int o = 0; o < nops; ++o) {
+        for (int d = 0; d < in; ++d) v->strides[o][d] /= e;
+        v->offset[o] /= e;
+    }
+    return true;
+}
+
+}  // namespace heph

@@ -46,3 +46,28 @@ bool layout_is_dense(const heph_layout &l);
 bool layout_covers_dense_block(const heph_layout &l, int64_t *first);
 
 }  // namespace heph
+
+namespace heph {
+
+// A view (or NOPS views of one shape, walked in lockstep) reshaped for
+// streaming by an order-insensitive fold: unit dims dropped, dims ordered by
+// the first operand's |stride| (largest outermost), dims where the first
+// operand's stride is negative flipped in every operand (the pairing of
+// elements is kept), and adjacent dims merged where every operand allows it.
+// A dense or permuted-dense block comes out as rank 1, stride 1.
+struct StreamView {
+    uint32_t rank = 0;  // 1..HEPH_MAX_RANK (an empty view never gets here)
+    uint64_t shape[HEPH_MAX_RANK] = {};
+    int64_t strides[2][HEPH_MAX_RANK] = {};
+    int64_t offset[2] = {};
+};
+void stream_view(const heph_layout *const *ls, int nops, StreamView *v);
+
+// Divides the innermost dim into 16-byte units of `elems` elements when every
+// operand's innermost stride is 1, its extent, the other strides and the
+// offsets are multiples of `elems`, and every operand's first element address
+// (base + offset) is 16-byte aligned.  Returns false and leaves *v unchanged
+// otherwise.
+bool stream_view_vectorize(StreamView *v, int nops, uint32_t elems, const void *const *bases, size_t elem_size);
+
+}  // namespace heph

@@ -10,18 +10,26 @@
 //     then a shared-memory fold of the warp results;
 //   * per-CTA partial to the stream's workspace, atomic ticket, and the last
 //     CTA folds the partials in CTA order and writes the scalar in place.
-// Non-dense views (transposed, diagonal, negative strides; rank <= 4) take a
-// grid-stride kernel that decodes each logical index with the view's strides
-// and feeds the same fold/finalize.
+// Other views (sub-blocks with gaps, diagonals, broadcasts, negative strides;
+// rank <= 4) are canonicalised on the host (unit dims dropped, negative
+// strides flipped, dims ordered by stride and merged) and walked by a kernel
+// that steps each thread's coordinates by the grid stride in the view's mixed
+// radix — no division per element, coalesced along a unit-stride inner dim,
+// 128-bit loads when the inner runs are 16-byte aligned.  The reference copies
+// such a view into a contiguous staging buffer first
+// (full_reduction_seam.rs:96-104).
 #include <algorithm>
 
 #include "device_utils.cuh"
 #include "kernels.h"
+#include "view_walk.cuh"
 
 namespace heph {
 
 constexpr int kReduceThreads = 256;
 constexpr int kReduceUnroll = 4;
+// Unaligned unit-stride runs at least this long take the row-run kernel.
+constexpr uint64_t kMinRunLength = 128;
 
 template <typename Tin, typename Tacc, int OP>
 __device__ __forceinline__ Tacc fold_vec(Tacc acc, uint4 raw) {
@@ -122,11 +130,99 @@ __global__ void __launch_bounds__(kReduceThreads)
     finish_grid<Tacc, OP>(acc, out, partials, ticket, scratch);
 }
 
+// Canonical strided view, walked without division (view_walk.cuh).  `n`
+// counts walk units: elements, or 16-byte vectors when VEC.
+template <typename Tin, typename Tacc, int OP, int R, bool VEC>
+__global__ void __launch_bounds__(kReduceThreads)
+    reduce_walk_kernel(const Tin *__restrict__ base, const ViewWalk<1> w, uint64_t n, Tacc *__restrict__ out,
+                       Tacc *__restrict__ partials, unsigned int *__restrict__ ticket) {
+    __shared__ Tacc scratch[kReduceThreads / 32];
+    const uint64_t stride = (uint64_t)gridDim.x * kReduceThreads;
+    uint64_t i = (uint64_t)blockIdx.x * kReduceThreads + threadIdx.x;
+    Tacc acc = identity<Tacc, OP>();
+    ViewCursor<R, 1> cur;
+    if (i < n) cur.seek(w, i);
+    auto fold_at = [&](int64_t o) {
+        if constexpr (VEC) acc = fold_vec<Tin, Tacc, OP>(acc, ld_stream(reinterpret_cast<const uint4 *>(base) + o));
+        else acc = combine<Tacc, OP>(acc, (Tacc)__ldg(base + o));
+    };
+    for (; i + (kReduceUnroll - 1) * stride < n; i += kReduceUnroll * stride) {
+        if constexpr (VEC) {
+            uint4 r[kReduceUnroll];
+#pragma unroll
+            for (int u = 0; u < kReduceUnroll; ++u) {
+                r[u] = ld_stream(reinterpret_cast<const uint4 *>(base) + cur.off[0]);
+                cur.advance(w);
+            }
+#pragma unroll
+            for (int u = 0; u < kReduceUnroll; ++u) acc = fold_vec<Tin, Tacc, OP>(acc, r[u]);
+        } else {
+            Tin r[kReduceUnroll];
+#pragma unroll
+            for (int u = 0; u < kReduceUnroll; ++u) {
+                r[u] = __ldg(base + cur.off[0]);
+                cur.advance(w);
+            }
+#pragma unroll
+            for (int u = 0; u < kReduceUnroll; ++u) acc = combine<Tacc, OP>(acc, (Tacc)r[u]);
+        }
+    }
+    for (; i < n; i += stride) {
+        fold_at(cur.off[0]);
+        cur.advance(w);
+    }
+    finish_grid<Tacc, OP>(acc, out, partials, ticket, scratch);
+}
+
+// Unit-stride runs that are not 16-byte aligned: warp per (run, segment),
+// scalar head/tail, 128-bit middle (view_walk.cuh RunWalk).
+template <typename Tin, typename Tacc, int OP>
+__global__ void __launch_bounds__(kReduceThreads)
+    reduce_runs_kernel(const Tin *__restrict__ base, const RunWalk w, Tacc *__restrict__ out,
+                       Tacc *__restrict__ partials, unsigned int *__restrict__ ticket) {
+    __shared__ Tacc scratch[kReduceThreads / 32];
+    Tacc acc = identity<Tacc, OP>();
+    run_walk_fold<Tin, 2 * kReduceUnroll>(base, w, acc, [](Tacc &a, Tin x) { a = combine<Tacc, OP>(a, (Tacc)x); });
+    finish_grid<Tacc, OP>(acc, out, partials, ticket, scratch);
+}
+
 template <typename Tacc, int OP> __global__ void write_identity_kernel(Tacc *out) {
     *out = identity<Tacc, OP>();
 }
 
 // ------------------------------------------------------------------ launch
+
+// Launches reduce_walk_kernel for a non-dense view; false (nothing launched)
+// when an inner dim of the canonical view exceeds 32-bit coordinates.
+template <typename Tin, typename Tacc, int OP>
+static bool launch_walk(cudaStream_t stream, const Tin *base, const heph_layout &l, uint64_t count, unsigned grid,
+                        Tacc *out, Tacc *partials, unsigned int *tickets) {
+    StreamView sv;
+    const heph_layout *ls[1] = {&l};
+    stream_view(ls, 1, &sv);
+    constexpr uint32_t V = 16 / sizeof(Tin);
+    const void *bases[1] = {base};
+    const bool vec = sv.rank >= 2 && stream_view_vectorize(&sv, 1, V, bases, sizeof(Tin));
+    RunWalk runs;
+    if (!vec && make_run_walk(sv, sizeof(Tin), kMinRunLength, &runs)) {
+        reduce_runs_kernel<Tin, Tacc, OP><<<grid, kReduceThreads, 0, stream>>>(base, runs, out, partials, tickets);
+        return true;
+    }
+    const uint64_t units = vec ? count / V : count;
+    const int R = sv.rank == 1 ? 1 : sv.rank == 2 ? 2 : 4;
+    ViewWalk<1> w;
+    if (!make_walk<1>(sv, R, (uint64_t)grid * kReduceThreads, &w)) return false;
+    const dim3 g(grid), b(kReduceThreads);
+    if (vec) {
+        if (R == 2) reduce_walk_kernel<Tin, Tacc, OP, 2, true><<<g, b, 0, stream>>>(base, w, units, out, partials, tickets);
+        else reduce_walk_kernel<Tin, Tacc, OP, 4, true><<<g, b, 0, stream>>>(base, w, units, out, partials, tickets);
+    } else {
+        if (R == 1) reduce_walk_kernel<Tin, Tacc, OP, 1, false><<<g, b, 0, stream>>>(base, w, units, out, partials, tickets);
+        else if (R == 2) reduce_walk_kernel<Tin, Tacc, OP, 2, false><<<g, b, 0, stream>>>(base, w, units, out, partials, tickets);
+        else reduce_walk_kernel<Tin, Tacc, OP, 4, false><<<g, b, 0, stream>>>(base, w, units, out, partials, tickets);
+    }
+    return true;
+}
 
 template <typename Tin, typename Tacc, int OP>
 static heph_status launch_typed(Device *dev, cudaStream_t stream, const void *base_v,
@@ -156,7 +252,7 @@ static heph_status launch_typed(Device *dev, cudaStream_t stream, const void *ba
         // order-insensitive, so the block streams contiguously.
         reduce_dense_kernel<Tin, Tacc, OP><<<grid, kReduceThreads, 0, stream>>>(
             base + (dense ? (int64_t)l.offset : first), count, out, partials, ws->tickets);
-    } else {
+    } else if (!launch_walk<Tin, Tacc, OP>(stream, base, l, count, grid, out, partials, ws->tickets)) {
         StridedView4 v{};
         v.rank = l.rank;
         for (uint32_t d = 0; d < l.rank; ++d) {

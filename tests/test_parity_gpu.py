@@ -419,3 +419,124 @@ def test_permuted_dense_views_full_reduction(device, oracle, dt):
             assert abs(float(got) - float(want)) <= 1e-5 * float(np.abs(x).sum())
         else:
             assert got == want
+
+
+# Gapped N-D views: sub-blocks with row gaps (16-byte aligned inner runs and
+# not), rank 3 and 4 with mixed-sign strides, a broadcast (stride-0) dim, a
+# diagonal.  They take the division-free walk kernels.
+def gapped_views(n_storage):
+    views = [
+        Layout.try_new([300, 256], [260, 1], 4),                 # aligned rows with gaps
+        Layout.try_new([300, 255], [257, 1], 3),                 # unaligned rows
+        Layout.try_new([7, 33, 64], [4000, 100, 1], 8),          # rank 3, aligned runs
+        Layout.try_new([3, 5, 7, 11], [3000, -500, 60, 2], 2100),  # rank 4, negative and non-unit
+        Layout.try_new([100, 64], [0, 1], 16),                   # broadcast rows
+        Layout.try_new([64, 100], [1, 0], 16),                   # broadcast inner dim
+        Layout.try_new([300], [301], 0),                         # diagonal
+        Layout.try_new([2, 9, 1, 130], [40000, 4096, 7, 3], 12),  # unit dim dropped, stride-3 rows
+        # Unaligned unit-stride runs (the row-run kernels):
+        Layout.try_new([90, 1001], [1003, 1], 5),
+        Layout.try_new([77, 130], [131, 1], 2),
+        Layout.try_new([1000, 15], [16, 1], 3),                  # one-element gaps, rows straddle vectors
+        Layout.try_new([200, 250], [-251, 1], 199 * 251 + 9),    # reversed rows
+        Layout.try_new([10, 9000], [9001, 1], 3),                # runs of several segments
+        Layout.try_new([3, 4, 300], [20011, 1003, 1], 7),        # rank 3, unaligned runs
+    ]
+    for v in views:
+        lo = v.offset + sum(min(0, (s - 1) * st) for s, st in zip(v.shape, v.strides))
+        hi = v.offset + sum(max(0, (s - 1) * st) for s, st in zip(v.shape, v.strides))
+        assert 0 <= lo and hi < n_storage, v
+    return views
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_gapped_views_full_reduction(device, oracle, dt):
+    rng = np.random.default_rng(77)
+    n = 100_000
+    ops = CudaFullReductionOps()
+    out = device.alloc_zeroed(dt, 1)
+    for code, op in OPS.items():
+        x = rand(dt, n, rng, prod=code == 1)
+        buf = device.upload(x)
+        for v in gapped_views(n):
+            ops.reduce_full_into(op, device, StridedView(buf, v), StridedView(out, Layout.c_contiguous([1])))
+            want = oracle.reduce_full(x, v.shape, v.strides, v.offset, op=code)
+            assert_close(device.download_owned(out), np.array([want], dtype=dt), dt, x)
+
+
+def test_gapped_views_widening(device, oracle):
+    rng = np.random.default_rng(78)
+    ops = CudaFullReductionOps()
+    for src, dst in [(np.int32, np.int64), (np.float32, np.float64)]:
+        x = (rng.integers(-2**31, 2**31 - 1, size=100_000, dtype=np.int64).astype(np.int32) if src == np.int32
+             else rng.uniform(-1, 1, size=100_000).astype(np.float32))
+        buf = device.upload(x)
+        out = device.alloc_zeroed(dst, 1)
+        for v in gapped_views(x.size):
+            ops.reduce_full_into(SumOp, device, StridedView(buf, v), StridedView(out, Layout.c_contiguous([1])))
+            want = oracle.reduce_full(x, v.shape, v.strides, v.offset, out_dtype=dst)
+            got = device.download_owned(out)[0]
+            if src == np.int32:
+                assert got == want, v
+            else:
+                assert abs(float(got) - float(want)) <= 1e-12 * float(np.abs(x).sum()), v
+
+
+def test_gapped_view_large_and_wide_inner_dim(device):
+    """A broadcast inner dim beyond 32-bit coordinates (2 x (2^31 + 5) logical
+    elements over 2 stored ones) and a large gapped sub-block, checked by closed
+    forms."""
+    x = np.array([3, 4], dtype=np.uint32)
+    buf = device.upload(x)
+    out = device.alloc_zeroed(np.uint32, 1)
+    inner = (1 << 31) + 5
+    v = Layout.try_new([2, inner], [1, 0], 0)
+    CudaFullReductionOps().reduce_full_into(SumOp, device, StridedView(buf, v), StridedView(out, Layout.c_contiguous([1])))
+    assert int(device.download_owned(out)[0]) == (7 * inner) % (1 << 32)
+    CudaFullReductionOps().reduce_full_into(MaxOp, device, StridedView(buf, v), StridedView(out, Layout.c_contiguous([1])))
+    assert int(device.download_owned(out)[0]) == 4
+    # 8192 x 8000 of an 8192 x 8192 u32 matrix: every element i*8192+j, j<8000.
+    rows, cols, ld = 8192, 8000, 8192
+    big = np.arange(rows * ld, dtype=np.uint64).astype(np.uint32)
+    bb = device.upload(big)
+    CudaFullReductionOps().reduce_full_into(SumOp, device, StridedView(bb, Layout.try_new([rows, cols], [ld, 1], 0)),
+                                            StridedView(out, Layout.c_contiguous([1])))
+    i = np.arange(rows, dtype=np.uint64)
+    want = (cols * i * ld).sum() + rows * (cols * (cols - 1) // 2)
+    assert int(device.download_owned(out)[0]) == int(want) % (1 << 32)
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+@pytest.mark.parametrize("map_kind", [0, 1, 2, 3, 4])
+def test_gapped_views_map_reduction(device, oracle, dt, map_kind):
+    import hephaestus_b200.seams as S
+    if map_kind == 3 and np.dtype(dt).kind != "f":
+        pytest.skip("norm_l2 is defined for floating-point types")
+    rng = np.random.default_rng(80 + map_kind)
+    n = 100_000
+    x, y = rand(dt, n, rng), rand(dt, n, rng)
+    xb, yb = device.upload(x), device.upload(y)
+    out = device.alloc_zeroed(dt, 1)
+    views = gapped_views(n)
+    pairs = [(v, v) for v in views]
+    # Dot products of differently laid out operands: a sub-block against the
+    # transpose of another, a broadcast against a reversed run, both transposed.
+    pairs += [(Layout.try_new([300, 256], [260, 1], 4), Layout.try_new([300, 256], [1, 300], 7)),
+              (Layout.try_new([100, 64], [0, 1], 16), Layout.try_new([100, 64], [-64, -1], 6399 + 20)),
+              (Layout.try_new([64, 210], [1, 64], 8), Layout.try_new([64, 210], [1, 64], 12))]
+    for la, lb in pairs:
+        S._map_call(device, map_kind, StridedView(xb, la), StridedView(yb, lb) if map_kind == 0 else None,
+                    StridedView(out, Layout.c_contiguous([1])))
+        xr, yr = (x.astype(np.float64), y.astype(np.float64)) if np.dtype(dt).kind == "f" and map_kind != 4 else (x, y)
+        want = oracle.map_reduce(map_kind, xr, la.shape, la.strides, la.offset,
+                                 b=yr if map_kind == 0 else None, b_strides=lb.strides, b_offset=lb.offset)
+        got = device.download_owned(out)[0]
+        if np.dtype(dt).kind == "f":
+            t = {np.dtype(np.float32): 1e-5, np.dtype(np.float64): 1e-12}[np.dtype(dt)]
+            # Bounds the view's terms: no view here repeats an element more
+            # than 100 times, and the buffers hold 10^5 terms of magnitude <= 1.
+            scale = float(np.abs(x.astype(np.float64) * (np.abs(y) if map_kind == 0 else 1)).sum()) \
+                if map_kind != 3 else float(np.sqrt((x.astype(np.float64) ** 2).sum()) * 10)
+            assert abs(float(got) - float(want)) <= t * max(scale, 1.0), (la, lb, got, want)
+        else:
+            assert got == want, (la, lb)
