@@ -8,6 +8,7 @@
 #include <cstring>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -795,11 +796,53 @@ extern "C" heph_status heph_prepared_free(heph_prepared *prepared) {
 // application/prepared_reduction.rs:165; submit_prepared_axis_reduction_batch,
 // prepared_axis_reduction.rs:84).  Scans are not batchable: each scan launch
 // carries the epoch tag of its tile status, which a replayed graph would reuse.
+//
+// Consecutive dense full reductions of one operator and element type are
+// fused into ONE kernel node (reduce_fused_kernel): the resident CTAs are
+// shared out over the problems, so a batch of small reductions streams at
+// HBM speed instead of paying a launch and a serial finalize per item.  A run
+// is fused only while no output of it overlaps an input of it or another of
+// its outputs, so the result equals running the items in order.
+namespace {
+
+struct Segment {
+    uint32_t first = 0, count = 1;  // items [first, first + count)
+    bool fused = false;
+    uint32_t grid = 0;
+    size_t table_off = 0, partials_off = 0, tickets_off = 0;  // into heph_batch::fused_mem
+};
+
+struct ByteRange {
+    uintptr_t lo, hi;
+    bool overlaps(const ByteRange &o) const { return lo < o.hi && o.lo < hi; }
+};
+
+// The dense run a full reduction reads, or false when its view is not one.
+bool fusable_full(const Call &c, FusedFull *f, ByteRange *in, ByteRange *out) {
+    if (c.kind != Kind::Full || c.noop || c.count == 0) return false;
+    int64_t first = 0;
+    if (layout_is_dense(c.in_l)) first = (int64_t)c.in_l.offset;
+    else if (!layout_covers_dense_block(c.in_l, &first)) return false;
+    const size_t es = dtype_size(c.in->dtype), os = dtype_size(c.out->dtype);
+    f->in = static_cast<const char *>(c.in->ptr) + first * (int64_t)es;
+    f->n = c.count;
+    f->out = static_cast<char *>(c.out->ptr) + c.out_l.offset * os;
+    in->lo = reinterpret_cast<uintptr_t>(f->in);
+    in->hi = in->lo + c.count * es;
+    out->lo = reinterpret_cast<uintptr_t>(f->out);
+    out->hi = out->lo + os;
+    return true;
+}
+
+}  // namespace
+
 struct heph_batch {
     heph_device *device = nullptr;
     cudaStream_t capture = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
+    std::vector<Segment> segments;
+    void *fused_mem = nullptr;  // fused runs' tables, partials and tickets
 };
 
 extern "C" heph_status heph_batch_create(heph_device *device, const heph_prepared *const *items, uint32_t count,
@@ -821,22 +864,101 @@ extern "C" heph_status heph_batch_create(heph_device *device, const heph_prepare
         if (b->exec) cudaGraphExecDestroy(b->exec);
         if (b->graph) cudaGraphDestroy(b->graph);
         if (b->capture) cudaStreamDestroy(b->capture);
+        if (b->fused_mem) cudaFree(b->fused_mem);
         delete b;
         return s;
     };
+
+    // Segments: maximal hazard-free runs of fusable full reductions sharing
+    // (operator, input type, output type); everything else one item each.
+    std::vector<std::vector<FusedFull>> tables;
+    for (uint32_t i = 0; i < count;) {
+        Segment seg;
+        seg.first = i;
+        FusedFull f{};
+        ByteRange rin{}, rout{};
+        if (fusable_full(items[i]->call, &f, &rin, &rout)) {
+            const Call &c0 = items[i]->call;
+            std::vector<FusedFull> table{f};
+            std::vector<ByteRange> ins{rin}, outs{rout};
+            uint32_t j = i + 1;
+            for (; j < count; ++j) {
+                const Call &c = items[j]->call;
+                if (c.op != c0.op || c.in->dtype != c0.in->dtype || c.out->dtype != c0.out->dtype) break;
+                if (!fusable_full(c, &f, &rin, &rout)) break;
+                bool hazard = rout.overlaps(rin);
+                for (size_t k = 0; k < ins.size() && !hazard; ++k)
+                    hazard = rout.overlaps(ins[k]) || rout.overlaps(outs[k]) || outs[k].overlaps(rin);
+                if (hazard) break;
+                table.push_back(f);
+                ins.push_back(rin);
+                outs.push_back(rout);
+            }
+            if (j - i >= 2) {
+                seg.count = j - i;
+                seg.fused = true;
+                tables.push_back(std::move(table));
+            }
+        }
+        i = seg.first + seg.count;
+        b->segments.push_back(seg);
+    }
+    if (!tables.empty()) {
+        auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+        size_t bytes = 0, t = 0;
+        for (Segment &seg : b->segments) {
+            if (!seg.fused) continue;
+            std::vector<FusedFull> &table = tables[t++];
+            seg.grid = plan_reduce_full_fused(device, items[seg.first]->call.in->dtype, table.data(), seg.count);
+            seg.table_off = bytes;
+            bytes += up(seg.count * sizeof(FusedFull));
+            seg.partials_off = bytes;
+            bytes += up((size_t)seg.grid * sizeof(double));
+            seg.tickets_off = bytes;
+            bytes += up(seg.count * sizeof(unsigned int));
+        }
+        if (cudaMalloc(&b->fused_mem, bytes) != cudaSuccess)
+            return cleanup(cuda_fail(HEPH_ALLOCATION_FAILED, cudaGetLastError(), "batch tables"));
+        if (cudaMemset(b->fused_mem, 0, bytes) != cudaSuccess)
+            return cleanup(cuda_fail(HEPH_DISPATCH_FAILED, cudaGetLastError(), "batch tables"));
+        t = 0;
+        for (Segment &seg : b->segments) {
+            if (!seg.fused) continue;
+            std::vector<FusedFull> &table = tables[t++];
+            if (cudaMemcpy(static_cast<char *>(b->fused_mem) + seg.table_off, table.data(),
+                           seg.count * sizeof(FusedFull), cudaMemcpyHostToDevice) != cudaSuccess)
+                return cleanup(cuda_fail(HEPH_TRANSFER_FAILED, cudaGetLastError(), "batch tables"));
+        }
+    }
+    auto enqueue = [&](cudaStream_t s) -> heph_status {
+        for (const Segment &seg : b->segments) {
+            heph_status r;
+            if (seg.fused) {
+                const Call &c = items[seg.first]->call;
+                char *m = static_cast<char *>(b->fused_mem);
+                r = launch_reduce_full_fused(s, c.op, c.in->dtype, c.out->dtype,
+                                             reinterpret_cast<const FusedFull *>(m + seg.table_off), seg.count,
+                                             seg.grid, m + seg.partials_off,
+                                             reinterpret_cast<unsigned int *>(m + seg.tickets_off));
+            } else {
+                r = run(device, items[seg.first]->call, s);
+            }
+            if (r != HEPH_OK) return r;
+        }
+        return HEPH_OK;
+    };
+
     if (cudaStreamCreateWithFlags(&b->capture, cudaStreamNonBlocking) != cudaSuccess)
         return cleanup(cuda_fail(HEPH_DISPATCH_FAILED, cudaGetLastError(), "batch stream"));
     // One eager pass sets up the capture stream's workspace, so that the
     // captured launches allocate nothing.
-    for (uint32_t i = 0; i < count; ++i) {
-        st = run(device, items[i]->call, b->capture);
-        if (st != HEPH_OK) return cleanup(st);
-    }
+    st = enqueue(b->capture);
+    if (st != HEPH_OK) return cleanup(st);
     if (cudaStreamSynchronize(b->capture) != cudaSuccess)
         return cleanup(cuda_fail(HEPH_DISPATCH_FAILED, cudaGetLastError(), "batch warm-up"));
     if (cudaStreamBeginCapture(b->capture, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
         return cleanup(cuda_fail(HEPH_DISPATCH_FAILED, cudaGetLastError(), "batch capture"));
-    for (uint32_t i = 0; i < count && st == HEPH_OK; ++i) st = run(device, items[i]->call, b->capture);
+    st = enqueue(b->capture);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(b->capture, &g);
     b->graph = g;
@@ -865,6 +987,10 @@ extern "C" heph_status heph_batch_free(heph_batch *batch) {
     if (batch->capture) {
         cudaStreamSynchronize(batch->capture);
         cudaStreamDestroy(batch->capture);
+    }
+    if (batch->fused_mem) {
+        cudaDeviceSynchronize();  // a replay on another stream may still read the tables
+        cudaFree(batch->fused_mem);
     }
     delete batch;
     return HEPH_OK;

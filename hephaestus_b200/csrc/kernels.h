@@ -17,6 +17,27 @@ heph_status launch_reduce_full(Device *dev, cudaStream_t stream, int op, heph_dt
                                heph_dtype acc_dtype, const void *base, const heph_layout &layout,
                                uint64_t count, void *out);
 
+// One problem of a fused batch of dense full reductions: `in` points at the
+// first element of a dense run of n elements, `out` at the output element.
+// cta_begin / ctas are filled by plan_reduce_full_fused.
+struct FusedFull {
+    const void *in;
+    uint64_t n;
+    void *out;
+    uint32_t cta_begin;
+    uint32_t ctas;
+};
+
+// Splits the resident-CTA budget of `dev` over the problems (all of
+// in_dtype); returns the grid size (sum of ctas) = partial slots needed.
+uint32_t plan_reduce_full_fused(const Device *dev, heph_dtype in_dtype, FusedFull *table, uint32_t nprob);
+
+// One launch for the whole table (device copy); partials: grid x acc-size
+// bytes, tickets: nprob zeroed words, both owned by the caller.
+heph_status launch_reduce_full_fused(cudaStream_t stream, int op, heph_dtype in_dtype, heph_dtype acc_dtype,
+                                     const FusedFull *table, uint32_t nprob, uint32_t grid, void *partials,
+                                     unsigned int *tickets);
+
 // Rank-2 axis reduction.  `mean` divides the sum by the axis length;
 // `indices` (u32, same layout as out) selects the arg-reduction form.
 heph_status launch_reduce_axis(Device *dev, cudaStream_t stream, int op, heph_dtype dtype,

@@ -39,28 +39,29 @@ __device__ __forceinline__ Tacc fold_vec(Tacc acc, uint4 raw) {
     return acc;
 }
 
-// Folds the block's value into the output: per-CTA partial, ticket, last
-// CTA folds all partials in CTA order.
+// Folds the block's value into the output of a slice of `nblocks` CTAs (this
+// one is `block` of them): per-CTA partial, ticket, and the slice's last CTA
+// folds the slice's partials in CTA order and writes the output in place.
 template <typename Tacc, int OP>
-__device__ __forceinline__ void finish_grid(Tacc acc, Tacc *out, Tacc *partials,
-                                            unsigned int *ticket, Tacc *scratch) {
+__device__ __forceinline__ void finish_slice(Tacc acc, Tacc *out, Tacc *partials, unsigned int *ticket,
+                                             unsigned int block, unsigned int nblocks, Tacc *scratch) {
     acc = block_fold<Tacc, OP, kReduceThreads>(acc, scratch);
-    if (gridDim.x == 1) {
+    if (nblocks == 1) {
         if (threadIdx.x == 0) *out = acc;
         return;
     }
     __shared__ bool am_last;
     if (threadIdx.x == 0) {
-        partials[blockIdx.x] = acc;
+        partials[block] = acc;
         __threadfence();
         unsigned int t = atomicAdd(ticket, 1u);
-        am_last = (t == gridDim.x - 1);
+        am_last = (t == nblocks - 1);
     }
     __syncthreads();
     if (!am_last) return;
     __threadfence();
     Tacc a = identity<Tacc, OP>();
-    for (unsigned int j = threadIdx.x; j < gridDim.x; j += kReduceThreads)
+    for (unsigned int j = threadIdx.x; j < nblocks; j += kReduceThreads)
         a = combine<Tacc, OP>(a, ld_cg(partials + j));
     a = block_fold<Tacc, OP, kReduceThreads>(a, scratch);
     if (threadIdx.x == 0) {
@@ -69,14 +70,21 @@ __device__ __forceinline__ void finish_grid(Tacc acc, Tacc *out, Tacc *partials,
     }
 }
 
+template <typename Tacc, int OP>
+__device__ __forceinline__ void finish_grid(Tacc acc, Tacc *out, Tacc *partials,
+                                            unsigned int *ticket, Tacc *scratch) {
+    finish_slice<Tacc, OP>(acc, out, partials, ticket, blockIdx.x, gridDim.x, scratch);
+}
+
+// This thread's fold of a dense run of n elements read by a slice of
+// `nblocks` CTAs (this one is `block`): 128-bit streaming loads, 4 in flight,
+// scalar head and tail around the 16-byte-aligned middle.
 template <typename Tin, typename Tacc, int OP>
-__global__ void __launch_bounds__(kReduceThreads)
-    reduce_dense_kernel(const Tin *__restrict__ in, uint64_t n, Tacc *__restrict__ out,
-                        Tacc *__restrict__ partials, unsigned int *__restrict__ ticket) {
-    __shared__ Tacc scratch[kReduceThreads / 32];
+__device__ __forceinline__ Tacc dense_fold(const Tin *__restrict__ in, uint64_t n, unsigned int block,
+                                           unsigned int nblocks) {
     constexpr int V = Vec16<Tin>::V;
-    const uint64_t tid = (uint64_t)blockIdx.x * kReduceThreads + threadIdx.x;
-    const uint64_t stride = (uint64_t)gridDim.x * kReduceThreads;
+    const uint64_t tid = (uint64_t)block * kReduceThreads + threadIdx.x;
+    const uint64_t stride = (uint64_t)nblocks * kReduceThreads;
 
     // Elements before the first 16-byte boundary and after the last one.
     const uintptr_t addr = reinterpret_cast<uintptr_t>(in);
@@ -98,8 +106,44 @@ __global__ void __launch_bounds__(kReduceThreads)
     for (; i < nvec; i += stride) acc = fold_vec<Tin, Tacc, OP>(acc, ld_stream(vin + i));
     if (tid < head) acc = combine<Tacc, OP>(acc, (Tacc)in[tid]);
     if (tid < n - tail) acc = combine<Tacc, OP>(acc, (Tacc)in[tail + tid]);
+    return acc;
+}
 
+template <typename Tin, typename Tacc, int OP>
+__global__ void __launch_bounds__(kReduceThreads)
+    reduce_dense_kernel(const Tin *__restrict__ in, uint64_t n, Tacc *__restrict__ out,
+                        Tacc *__restrict__ partials, unsigned int *__restrict__ ticket) {
+    __shared__ Tacc scratch[kReduceThreads / 32];
+    const Tacc acc = dense_fold<Tin, Tacc, OP>(in, n, blockIdx.x, gridDim.x);
     finish_grid<Tacc, OP>(acc, out, partials, ticket, scratch);
+}
+
+// A fused batch of dense full reductions in one launch: problem p owns CTAs
+// [cta_begin, cta_begin + ctas) of the grid, its own partial slots (indexed
+// like its CTAs) and ticket; a CTA finds its problem by binary search over
+// the table's cta_begin.
+template <typename Tin, typename Tacc, int OP>
+__global__ void __launch_bounds__(kReduceThreads)
+    reduce_fused_kernel(const FusedFull *__restrict__ table, uint32_t nprob, Tacc *__restrict__ partials,
+                        unsigned int *__restrict__ tickets) {
+    __shared__ Tacc scratch[kReduceThreads / 32];
+    __shared__ uint32_t s_prob;
+    if (threadIdx.x == 0) {
+        uint32_t lo = 0, hi = nprob - 1;
+        while (lo < hi) {
+            const uint32_t mid = (lo + hi + 1) / 2;
+            if (table[mid].cta_begin <= blockIdx.x) lo = mid;
+            else hi = mid - 1;
+        }
+        s_prob = lo;
+    }
+    __syncthreads();
+    const uint32_t p = s_prob;
+    const FusedFull f = table[p];
+    const unsigned int block = blockIdx.x - f.cta_begin;
+    const Tacc acc = dense_fold<Tin, Tacc, OP>(static_cast<const Tin *>(f.in), f.n, block, f.ctas);
+    finish_slice<Tacc, OP>(acc, static_cast<Tacc *>(f.out), partials + f.cta_begin, tickets + p, block, f.ctas,
+                           scratch);
 }
 
 struct StridedView4 {
@@ -294,6 +338,50 @@ heph_status launch_reduce_full(Device *dev, cudaStream_t stream, int op, heph_dt
     return fail(HEPH_INVALID_CONFIGURATION,
                 "full reduction output type must match the input type or widen it (i32->i64, "
                 "f32->f64)");
+}
+
+uint32_t plan_reduce_full_fused(const Device *dev, heph_dtype in_dtype, FusedFull *table, uint32_t nprob) {
+    const uint64_t per_cta = (uint64_t)kReduceThreads * kReduceUnroll * (16 / dtype_size(in_dtype));
+    const uint64_t cap = (uint64_t)dev->sm_count * (2048 / kReduceThreads);
+    uint64_t want_total = 0, n_total = 0;
+    for (uint32_t p = 0; p < nprob; ++p) {
+        want_total += std::max<uint64_t>(1, (table[p].n + per_cta - 1) / per_cta);
+        n_total += table[p].n;
+    }
+    uint32_t next = 0;
+    for (uint32_t p = 0; p < nprob; ++p) {
+        const uint64_t want = std::max<uint64_t>(1, (table[p].n + per_cta - 1) / per_cta);
+        // Within the resident-CTA budget every problem gets its own grid's
+        // worth; beyond it, CTAs in proportion to the elements.
+        const uint64_t c = want_total <= cap ? want
+                                             : std::max<uint64_t>(1, std::min(want, cap * table[p].n / std::max<uint64_t>(1, n_total)));
+        table[p].cta_begin = next;
+        table[p].ctas = (uint32_t)c;
+        next += (uint32_t)c;
+    }
+    return next;
+}
+
+heph_status launch_reduce_full_fused(cudaStream_t stream, int op, heph_dtype in_dtype, heph_dtype acc_dtype,
+                                     const FusedFull *table, uint32_t nprob, uint32_t grid, void *partials,
+                                     unsigned int *tickets) {
+    auto go = [&]<typename Tin, typename Tacc>() -> heph_status {
+        Tacc *pp = static_cast<Tacc *>(partials);
+        switch (op) {
+            case OP_SUM: reduce_fused_kernel<Tin, Tacc, OP_SUM><<<grid, kReduceThreads, 0, stream>>>(table, nprob, pp, tickets); break;
+            case OP_PROD: reduce_fused_kernel<Tin, Tacc, OP_PROD><<<grid, kReduceThreads, 0, stream>>>(table, nprob, pp, tickets); break;
+            case OP_MIN: reduce_fused_kernel<Tin, Tacc, OP_MIN><<<grid, kReduceThreads, 0, stream>>>(table, nprob, pp, tickets); break;
+            case OP_MAX: reduce_fused_kernel<Tin, Tacc, OP_MAX><<<grid, kReduceThreads, 0, stream>>>(table, nprob, pp, tickets); break;
+            default: return fail(HEPH_INVALID_CONFIGURATION, "full reduction supports sum, prod, min and max");
+        }
+        HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "fused full reduction launch");
+        return HEPH_OK;
+    };
+    if (in_dtype == acc_dtype)
+        return dispatch_dtype(in_dtype, [&]<typename T>() { return go.template operator()<T, T>(); });
+    if (in_dtype == HEPH_I32 && acc_dtype == HEPH_I64) return go.template operator()<int32_t, int64_t>();
+    if (in_dtype == HEPH_F32 && acc_dtype == HEPH_F64) return go.template operator()<float, double>();
+    return fail(HEPH_INVALID_CONFIGURATION, "full reduction output type must match the input type or widen it");
 }
 
 }  // namespace heph

@@ -315,8 +315,11 @@ heph_status heph_prepared_free(heph_prepared *prepared);
  * application/prepared_reduction.rs:165) and submit_prepared_axis_reduction_batch
  * (prepared_axis_reduction.rs:84): a fixed list of prepared full / axis
  * reductions recorded once as a CUDA graph and replayed with one launch per
- * heph_batch_launch.  Creation dispatches every item once (setting up the
- * workspace the graph uses).  Replays of one batch must not overlap on the GPU.
+ * heph_batch_launch.  Consecutive dense full reductions of one operator and
+ * element type whose outputs overlap none of the run's inputs or other
+ * outputs are fused into one kernel (same results as running them in order).
+ * Creation dispatches every item once (setting up the workspace the graph
+ * uses).  Replays of one batch must not overlap on the GPU.
  * Prepared scans are rejected (InvalidConfiguration). */
 typedef struct heph_batch heph_batch;
 heph_status heph_batch_create(heph_device *device, const heph_prepared *const *items, uint32_t count,

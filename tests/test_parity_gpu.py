@@ -540,3 +540,70 @@ def test_gapped_views_map_reduction(device, oracle, dt, map_kind):
             assert abs(float(got) - float(want)) <= t * max(scale, 1.0), (la, lb, got, want)
         else:
             assert got == want, (la, lb)
+
+
+# Batches: runs of dense full reductions of one operator and type are fused
+# into one kernel; the results must equal running the items in order.
+@pytest.mark.parametrize("dt", [np.float32, np.int32, np.uint32, np.float64, np.int64])
+def test_fused_batch_of_full_reductions(device, oracle, dt):
+    import hephaestus_b200.seams as S
+    rng = np.random.default_rng(90)
+    sizes = [1, 3, 31, 4096, 4099, 100_003, 1 << 20, 2_000_001, 7, 65536]
+    xs = [rand(dt, n, rng) for n in sizes]
+    bufs = [device.upload(x) for x in xs]
+    out = device.alloc_zeroed(dt, 3 * len(sizes))
+    ops = CudaFullReductionOps()
+    items, want = [], []
+    # run 1: sums over every buffer (unaligned offsets on some), run 2: max,
+    # run 3: a permuted dense view and a reversed one (dense blocks).
+    for k, (x, b) in enumerate(zip(xs, bufs)):
+        off = k % 3 if x.size > 3 else 0
+        lay = Layout.try_new([x.size - off], [1], off)
+        items.append(ops.prepare_reduce_full(SumOp, device, StridedView(b, lay),
+                                             StridedView(out, Layout.try_new([1], [1], k))))
+        want.append((k, oracle.reduce_full(x, lay.shape, lay.strides, lay.offset, op=0), x))
+    for k, (x, b) in enumerate(zip(xs, bufs)):
+        lay = Layout.c_contiguous([x.size])
+        items.append(ops.prepare_reduce_full(MaxOp, device, StridedView(b, lay),
+                                             StridedView(out, Layout.try_new([1], [1], len(sizes) + k))))
+        want.append((len(sizes) + k, oracle.reduce_full(x, [x.size], op=3), x))
+    x = xs[6]
+    for j, lay in enumerate([Layout.try_new([1024, 1024], [1, 1024], 0), Layout.try_new([1 << 20], [-1], (1 << 20) - 1)]):
+        items.append(ops.prepare_reduce_full(MaxOp, device, StridedView(bufs[6], lay),
+                                             StridedView(out, Layout.try_new([1], [1], 2 * len(sizes) + j))))
+        want.append((2 * len(sizes) + j, oracle.reduce_full(x, lay.shape, lay.strides, lay.offset, op=3), x))
+    batch = S.Batch(device, items)
+    for rep in range(3):  # replays reuse the tickets: they must come back to rest
+        device.write_buffer(out, np.zeros(3 * len(sizes), dtype=dt))
+        batch.launch()
+        got = device.download_owned(out)
+        for slot, w, xx in want:
+            assert_close(got[slot:slot + 1], np.array([w], dtype=dt), dt, xx)
+
+
+def test_fused_batch_widening_and_hazards(device, oracle):
+    import hephaestus_b200.seams as S
+    rng = np.random.default_rng(91)
+    ops = CudaFullReductionOps()
+    x = rng.integers(-2**31, 2**31 - 1, size=1_000_003, dtype=np.int64).astype(np.int32)
+    xb = device.upload(x)
+    o64 = device.alloc_zeroed(np.int64, 4)
+    one = lambda k: Layout.try_new([1], [1], k)  # noqa: E731
+    items = [ops.prepare_reduce_full(SumOp, device, StridedView(xb, Layout.try_new([n], [1], 0)),
+                                     StridedView(o64, one(k))) for k, n in enumerate([1_000_003, 5, 999_999, 64])]
+    S.Batch(device, items).launch()
+    got = device.download_owned(o64)
+    for k, n in enumerate([1_000_003, 5, 999_999, 64]):
+        assert got[k] == int(x[:n].astype(np.int64).sum())
+    # Read-after-write inside a run: item 2 sums the buffer item 1 writes
+    # into, item 3 writes the same element as item 1.  In order: s = sum(a);
+    # t = s + b[1]; u = max(b[0..1]) overwrites the element item 1 wrote.
+    a = device.upload(np.arange(1, 101, dtype=np.uint32))
+    b = device.upload(np.array([0, 7], dtype=np.uint32))
+    t = device.alloc_zeroed(np.uint32, 1)
+    it1 = ops.prepare_reduce_full(SumOp, device, StridedView(a, Layout.c_contiguous([100])), StridedView(b, one(0)))
+    it2 = ops.prepare_reduce_full(SumOp, device, StridedView(b, Layout.c_contiguous([2])), StridedView(t, one(0)))
+    it3 = ops.prepare_reduce_full(SumOp, device, StridedView(b, Layout.try_new([1], [1], 1)), StridedView(b, one(0)))
+    S.Batch(device, [it1, it2, it3]).launch()
+    assert device.download_owned(t)[0] == 5050 + 7
+    assert list(device.download_owned(b)) == [7, 7]
