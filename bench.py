@@ -216,6 +216,17 @@ def cpu_sample(cfg_id: int, cfg: dict, oracle, seconds: float = 10.0, threads: i
         f"column sum of [512 x 65536] f64 x {reps} reps"
 
 
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def run_reference(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -231,6 +242,10 @@ def run_reference(args, cfg):
         if i >= args.warmup:
             vals.append(v)
     value = statistics.median(vals)
+    # The reference's host device is single-threaded ("never a performance
+    # path"): that figure is reported beside the all-cores one.
+    single, _, single_desc = (value, cores, desc) if cores == 1 else \
+        cpu_sample(args.config, cfg, oracle, seconds=min(per_step, 5.0), threads=1)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -239,7 +254,9 @@ def run_reference(args, cfg):
         "config": {"workload": cfg["workload"], "config_index": args.config},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": desc + " per step (oracle restatement of the host reference semantics, "
-                                          + ("OpenMP over all cores)" if cores > 1 else "sequential strided fold)")},
+                                          + ("OpenMP over all cores)" if cores > 1 else "sequential strided fold)"),
+                         "single_thread_value": round(single, 3), "single_thread_sample": single_desc,
+                         "nproc": os.cpu_count(), "cpu_model": cpu_model()},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -474,6 +491,28 @@ def main():
     achieved = kernel_bytes / (kernel_ms / 1e3) / 1e9
     traffic = profiled_traffic(cfg["kernel"], args.config)
 
+    latency = None
+    if args.config == 1:
+        # Latency mode: one 4 MiB reduction on its own (reduce_dense_kernel),
+        # median of 20 event-timed calls over rotating buffers.  Each timed
+        # call is queued behind a ~50 us replay of the batch, so the events
+        # bracket the device's work and not the host's time to issue it.
+        ls, le = [], []
+        with torch.cuda.stream(stream):
+            for k in range(23):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                batch.launch(stream=sp)
+                a.record(stream)
+                ops.reduce_full_into(SumOp, dev, StridedView(bufs[k % nbuf], lay),
+                                     StridedView(out, Layout.try_new([1], [1], k % nbuf)), stream=sp)
+                b.record(stream)
+                ls.append(a)
+                le.append(b)
+        dev.synchronize_stream(sp)
+        us = statistics.median(a.elapsed_time(b) * 1e3 for a, b in list(zip(ls, le))[3:])
+        latency = {"us_per_reduction": round(us, 3), "kernel": "reduce_dense_kernel",
+                   "gbs": round(4 * n / (us / 1e6) / 1e9, 2)}
+
     # ---------------- end to end through the public API with host buffers -------------
     e2e = None
     if not args.no_e2e:
@@ -516,6 +555,7 @@ def main():
                          "launch_ms": round(kernel_ms, 6)},
             "cpu_baseline": cpu,
             "e2e": e2e,
+            **({"latency_mode": latency} if latency else {}),
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * args.steps,
         }

@@ -59,6 +59,7 @@ SIGNATURES = [
     ("heph_device_close", _st, [_vp]),
     ("heph_device_backend_name", ctypes.c_char_p, [_vp]),
     ("heph_device_synchronize", _st, [_vp]),
+    ("heph_selftest_wait_timeout", _st, [_vp, _i, _vp]),
     ("heph_stream_synchronize", _st, [_vp, _vp]),
     ("heph_device_stream", _st, [_vp, _pp]),
     ("heph_device_ordinal", _st, [_vp, ctypes.POINTER(_i)]),

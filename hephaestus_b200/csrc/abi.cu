@@ -255,6 +255,14 @@ extern "C" heph_status heph_device_synchronize(heph_device *device) {
     return heph_stream_synchronize(device, nullptr);
 }
 
+extern "C" heph_status heph_selftest_wait_timeout(heph_device *device, int which, heph_stream stream) {
+    if (!device) return fail(HEPH_INVALID_CONFIGURATION, "null device");
+    if (which != 0 && which != 1) return fail(HEPH_INVALID_CONFIGURATION, "unknown wait self-test");
+    heph_status st = bind(device);
+    if (st != HEPH_OK) return st;
+    return launch_wait_selftest(device, resolve_stream(device, stream), which);
+}
+
 extern "C" heph_status heph_device_stream(heph_device *device, heph_stream *out) {
     if (!device || !out) return fail(HEPH_INVALID_CONFIGURATION, "null argument");
     *out = device->stream;

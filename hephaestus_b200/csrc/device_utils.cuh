@@ -147,6 +147,13 @@ template <typename T> __device__ __forceinline__ uint4 as_uint4(const Vec16<T> &
     return bitcast<uint4>(v);
 }
 
+// Nanoseconds of the GPU's global timer (for time-bounded waits).
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 // Sets a device-side error bit visible to the host after synchronisation.
 __device__ __forceinline__ void raise_device_error(unsigned int *err, unsigned int code) {
     if (err) atomicOr(err, code);

@@ -50,6 +50,10 @@ heph_status launch_map_reduce(Device *dev, cudaStream_t stream, int map, heph_dt
                               const heph_layout &la, const void *b, const heph_layout &lb, uint64_t count,
                               void *out);
 
+// Bounded-wait self-test: 0 = look-back wait, 1 = staged-part mbarrier wait,
+// each against a partner that never arrives (raises the device error bit).
+heph_status launch_wait_selftest(Device *dev, cudaStream_t stream, int which);
+
 // Axis scan (rank 1 or 2).  `carry` (nullable, device) seeds line 0.
 heph_status launch_scan(Device *dev, cudaStream_t stream, int op, heph_dtype dtype,
                         const void *in, void *out, const AxisProblem &p, bool reverse,

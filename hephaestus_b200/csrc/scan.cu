@@ -404,16 +404,24 @@ __device__ __forceinline__ void bulk_load(void *dst_smem, const void *src, uint3
                  : "memory");
 }
 
-// Waits for phase `parity` of `bar`.  Bounded: after the poll budget the
-// device error bit is raised and the wait gives up.
+// Waits for phase `parity` of `bar`.  Bounded in time (kMbarWaitNs by the
+// global timer, checked every 64 polls): past it the device error bit is
+// raised and the wait gives up.
+constexpr uint64_t kMbarWaitNs = 2000000000ull;
 __device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, unsigned int *err) {
-    for (uint32_t polls = 0; polls < (1u << 26); ++polls) {
+    uint64_t start = 0;
+    for (uint32_t polls = 1;; ++polls) {
         uint32_t done;
         asm volatile("{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n selp.u32 %0, 1, 0, P;\n}"
                      : "=r"(done)
                      : "r"(smem_addr(bar)), "r"(parity)
                      : "memory");
         if (done) return;
+        if ((polls & 63u) == 0) {
+            const uint64_t now = globaltimer_ns();
+            if (start == 0) start = now;
+            else if (now - start > kMbarWaitNs) break;
+        }
     }
     if (threadIdx.x == 0) raise_device_error(err, DEVERR_BULK_TIMEOUT);
 }
@@ -713,6 +721,51 @@ static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *
         default: scan_lookback_kernel<T, OP, true, kLookbackVectors, true, true><<<grid, kScanThreads, 0, stream>>>(p); break;
     }
     HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "scan launch");
+    return HEPH_OK;
+}
+
+// ------------------------------------------------ bounded-wait self-test
+//
+// Runs the production waits against partners that never arrive: the
+// look-back wait on a predecessor tile that never publishes (0), or the
+// mbarrier wait of a staged part on a barrier nothing arrives on (1).  Each
+// gives up after its bound, raises its error bit and returns, so the host
+// sees the failure on its next synchronisation and the context stays usable.
+
+__global__ void lookback_timeout_selftest_kernel(StatusView status, unsigned int *err) {
+    LookbackParams<uint32_t> p{};
+    p.status = status;
+    p.err = err;
+    (void)lookback<uint32_t, OP_SUM>(p, 1, 0, threadIdx.x & 31);
+}
+
+__global__ void mbar_timeout_selftest_kernel(unsigned int *err) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    mbar_wait(&bar, 0, err);
+}
+
+heph_status launch_wait_selftest(Device *dev, cudaStream_t stream, int which) {
+    if (which == 1) {
+        mbar_timeout_selftest_kernel<<<1, 32, 0, stream>>>(dev->error_dev);
+        HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "wait self-test launch");
+        return HEPH_OK;
+    }
+    unsigned long long *packed = nullptr;
+    HEPH_CUDA_TRY(cudaMallocFromPoolAsync((void **)&packed, 2 * sizeof(unsigned long long), dev->pool, stream),
+                  HEPH_ALLOCATION_FAILED, "wait self-test status");
+    cudaMemsetAsync(packed, 0, 2 * sizeof(unsigned long long), stream);
+    StatusView sv{};
+    sv.epoch = 1;  // the zeroed entries carry epoch 0: never published
+    sv.packed = packed;
+    lookback_timeout_selftest_kernel<<<1, 32, 0, stream>>>(sv, dev->error_dev);
+    const cudaError_t e = cudaGetLastError();
+    cudaFreeAsync(packed, stream);
+    HEPH_CUDA_TRY(e, HEPH_DISPATCH_FAILED, "wait self-test launch");
     return HEPH_OK;
 }
 

@@ -132,6 +132,14 @@ const char *heph_device_backend_name(const heph_device *device);
  * stream and reports a device-side failure (e.g. a bounded look-back wait
  * that ran out) as DispatchFailed. */
 heph_status heph_device_synchronize(heph_device *device);
+/* Self-test of the failure path of the bounded device waits (no counterpart
+ * in the reference): enqueues the look-back wait (which = 0) or the
+ * staged-part mbarrier wait (which = 1) against a partner that never
+ * arrives.  The wait gives up after its bound (about a second for the
+ * look-back, two seconds for the mbarrier), raises the device error bit and
+ * returns; the next synchronize reports DispatchFailed and the device stays
+ * usable.  No GPU fault is involved. */
+heph_status heph_selftest_wait_timeout(heph_device *device, int which, heph_stream stream);
 /* Waits for `stream` and reports device-side failures like synchronize. */
 heph_status heph_stream_synchronize(heph_device *device, heph_stream stream);
 /* The device's own stream (a cudaStream_t). */
