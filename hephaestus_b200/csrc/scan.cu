@@ -227,6 +227,26 @@ __device__ __forceinline__ void load_tile_vec(const T *src, int base, T (&x)[JV]
     }
 }
 
+// A full tile from shared memory with explicit shared-space loads (a
+// generic pointer would be loaded through the global path's scoreboard).
+template <typename T, int JV>
+__device__ __forceinline__ void load_tile_smem(const T *src, int base, T (&x)[JV][ScanShape<T, JV>::V]) {
+    constexpr int V = ScanShape<T, JV>::V;
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(src + base);
+    uint4 raw[JV];
+#pragma unroll
+    for (int j = 0; j < JV; ++j)
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(raw[j].x), "=r"(raw[j].y), "=r"(raw[j].z), "=r"(raw[j].w)
+                     : "r"(a + (uint32_t)(j * 32 * V * sizeof(T))));
+#pragma unroll
+    for (int j = 0; j < JV; ++j) {
+        Vec16<T> e = as_elems<T>(raw[j]);
+#pragma unroll
+        for (int c = 0; c < V; ++c) x[j][c] = e.e[c];
+    }
+}
+
 // Guarded element loads of a partial (or unaligned) tile; identity padding.
 template <typename T, int OP, int JV>
 __device__ __forceinline__ void load_tile_scalar(const T *src, uint64_t valid, int base,
@@ -458,17 +478,40 @@ __device__ __forceinline__ void chunk_reduce_part(const ChunkParams<T> &p, int b
         const int k = (int)(c % p.buffers);
         mbar_wait(&bar[k], (phases >> k) & 1u, p.err);
         phases ^= 1u << k;
-        const uint4 *v = reinterpret_cast<const uint4 *>(buf + k * p.part);
-        for (uint64_t q = threadIdx.x; q < n / V; q += kScanThreads) {
-            Vec16<T> e = as_elems<T>(v[q]);
+        // Explicit shared-space loads, 32-bit offsets; the part is a whole
+        // number of 16 KiB tiles, so 1024 vectors per step divide it.
+        const uint32_t a0 = (uint32_t)__cvta_generic_to_shared(buf + k * p.part) + threadIdx.x * 16u;
+        const uint32_t nbytes = (uint32_t)(n * sizeof(T));
+#pragma unroll 2
+        for (uint32_t off = 0; off < nbytes; off += kScanThreads * 16u * 4u) {
+            uint4 r[4];
 #pragma unroll
-            for (int t = 0; t < V; ++t) acc = combine<T, OP>(acc, e.e[t]);
+            for (int u = 0; u < 4; ++u)
+                asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                             : "=r"(r[u].x), "=r"(r[u].y), "=r"(r[u].z), "=r"(r[u].w)
+                             : "r"(a0 + off + u * kScanThreads * 16u));
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                Vec16<T> e = as_elems<T>(r[u]);
+#pragma unroll
+                for (int t = 0; t < V; ++t) acc = combine<T, OP>(acc, e.e[t]);
+            }
         }
     } else {
         for (uint64_t e = lo + threadIdx.x; e < hi; e += kScanThreads) acc = combine<T, OP>(acc, p.in[e]);
     }
-    acc = block_fold<T, OP, kScanThreads>(acc, s_red);
-    if (threadIdx.x == 0) publish(p.status, c * gridDim.x + b, kStatePrefix, acc);
+    // Only thread 0 needs the CTA total: one barrier, no trailing one (the
+    // caller alternates s_red by chunk parity, and the reduces of chunks c and
+    // c + 2 are separated by barriers).
+    acc = warp_fold<T, OP>(acc);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        T r = s_red[0];
+#pragma unroll
+        for (int w = 1; w < kScanWarps; ++w) r = combine<T, OP>(r, s_red[w]);
+        publish(p.status, c * gridDim.x + b, kStatePrefix, r);
+    }
 }
 
 template <typename T, int OP, int JV, bool REV, bool EXCL>
@@ -479,8 +522,8 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
     T *buf = reinterpret_cast<T *>(dyn_smem);  // buffers x part elements
     __shared__ uint64_t bar[kChunkMaxBuffers];
     __shared__ T s_warp[2][kScanWarps];
-    __shared__ T s_red[kScanWarps];
-    __shared__ T s_red2[kScanWarps];
+    __shared__ T s_red[2][kScanWarps];  // by chunk parity: consecutive part reduces have no barrier between
+    __shared__ T s_pair[2][kScanWarps];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int G = gridDim.x, b = blockIdx.x;
     const int NB = p.buffers;
@@ -496,10 +539,26 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
     __syncthreads();
 
     T carry = p.carry ? *p.carry : identity<T, OP>();
-    if (p.nchunks > 0) chunk_reduce_part<T, OP>(p, b, 0, buf, bar, phases, s_red);
+    if (p.nchunks > 0) chunk_reduce_part<T, OP>(p, b, 0, buf, bar, phases, s_red[0]);
     int parity = 0;
     for (uint64_t c = 0; c < p.nchunks; ++c) {
-        if (c + 1 < p.nchunks) chunk_reduce_part<T, OP>(p, b, c + 1, buf, bar, phases, s_red);
+        // The part totals of chunk c were published one iteration ago: for
+        // 4-byte T their status words are loaded here, before the part
+        // reduce, so the L2 round trip overlaps it.
+        unsigned long long early[kChunkMaxPartsPerThread];
+        if constexpr (sizeof(T) == 4) {
+#pragma unroll
+            for (int i = 0; i < kChunkMaxPartsPerThread; ++i) {
+                const int q = threadIdx.x + i * kScanThreads;
+                early[i] = 0;
+                if (q < G)
+                    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];"
+                                 : "=l"(early[i])
+                                 : "l"(p.status.packed + c * G + q)
+                                 : "memory");
+            }
+        }
+        if (c + 1 < p.nchunks) chunk_reduce_part<T, OP>(p, b, c + 1, buf, bar, phases, s_red[(c + 1) & 1]);
 
         // Step 2: the part totals of chunk c.
         T before = identity<T, OP>(), total = identity<T, OP>();
@@ -508,7 +567,14 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
             const int q = threadIdx.x + i * kScanThreads;
             if (q >= G) break;
             T v = identity<T, OP>();
-            bool ok = read_status(p.status, c * G + q, v) != kStateInvalid;
+            bool ok;
+            if constexpr (sizeof(T) == 4) {
+                const uint32_t f = (uint32_t)early[i];
+                v = bitcast<T>((uint32_t)(early[i] >> 32));
+                ok = (f >> 2) == p.status.epoch && (f & 3u) != kStateInvalid;
+            } else {
+                ok = read_status(p.status, c * G + q, v) != kStateInvalid;
+            }
             uint32_t polls = 0;
             while (!ok) {
                 if (++polls > kPolls) {
@@ -522,8 +588,22 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
             total = combine<T, OP>(total, v);
             if (rev ? (q > b) : (q < b)) before = combine<T, OP>(before, v);
         }
-        before = block_fold<T, OP, kScanThreads>(before, s_red);
-        total = block_fold<T, OP, kScanThreads>(total, s_red2);
+        // Both folds share one barrier; s_pair is rewritten only in the next
+        // iteration, after the tile scans' barriers.
+        before = warp_fold<T, OP>(before);
+        total = warp_fold<T, OP>(total);
+        if (lane == 0) {
+            s_pair[0][warp] = before;
+            s_pair[1][warp] = total;
+        }
+        __syncthreads();
+        before = s_pair[0][0];
+        total = s_pair[1][0];
+#pragma unroll
+        for (int w = 1; w < kScanWarps; ++w) {
+            before = combine<T, OP>(before, s_pair[0][w]);
+            total = combine<T, OP>(total, s_pair[1][w]);
+        }
         T run = combine<T, OP>(carry, before);
         carry = combine<T, OP>(carry, total);
 
@@ -539,19 +619,26 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
             const uint64_t valid = min((uint64_t)TILE, hi - lo - start);
             const bool full = valid == (uint64_t)TILE;
             T x[JV][V];
-            if (full) load_tile_vec<T, JV>(src + start, base, x, false);
+            if (staged) load_tile_smem<T, JV>(src + start, base, x);
+            else if (full) load_tile_vec<T, JV>(src + start, base, x, false);
             else load_tile_scalar<T, OP, JV>(src + start, valid, base, x);
             TileScan<T, JV> r;
             tile_local_scan<T, OP, JV, REV>(x, s_warp[parity], r);
             parity ^= 1;
+            // Past the last tile's barrier every thread has read the part out
+            // of buffer c%NB: refill it with chunk c+NB now, so the copy is in
+            // flight while the last tile is finished and stored.
+            if (tl + 1 == ntiles && threadIdx.x == 0 && c + NB < p.nchunks) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                chunk_stage_in(p, b, c + NB, buf, bar);
+            }
             T y[JV][V];
             tile_outputs<T, OP, JV, REV, EXCL>(x, r, run, y);
             run = combine<T, OP>(run, r.agg);
             store_tile<T, JV>(p.out + lo + start, valid, full, base, y, p.store_mode);
         }
-        // Every thread is done with buffer c%NB: refill it with chunk c+NB.
-        __syncthreads();
-        if (threadIdx.x == 0 && c + NB < p.nchunks) chunk_stage_in(p, b, c + NB, buf, bar);
+        // An empty part (past the end of the line) never used its buffer.
+        if (ntiles == 0 && threadIdx.x == 0 && c + NB < p.nchunks) chunk_stage_in(p, b, c + NB, buf, bar);
     }
 }
 
