@@ -414,7 +414,7 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 }
 
 // Thread 0: expect `bytes` on `bar` and start a bulk global->shared copy
-// (no multicast; the source is this GPU's own memory).
+// (a plain bulk copy; the source is this GPU's own memory).
 __device__ __forceinline__ void bulk_load(void *dst_smem, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                  : "memory");
