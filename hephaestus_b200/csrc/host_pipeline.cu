@@ -9,6 +9,8 @@
 // chunk k-1, kept on the device by a one-thread kernel, so the result equals
 // the whole-buffer scan and no host synchronisation happens between chunks.
 #include <algorithm>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -24,6 +26,36 @@ __global__ void carry_after_chunk(const T *last_out, const T *last_in, int exclu
 }
 
 constexpr int kSlots = 3;
+
+// Piece boundaries of the pipeline: full chunks in the middle, and at each
+// end pieces of 1/8, 1/4, 1/2 chunk, so the lone first upload and the lone
+// last download (nothing to overlap them with) are short.
+std::vector<std::pair<uint64_t, uint64_t>> pipeline_pieces(uint64_t n, uint64_t chunk) {
+    std::vector<std::pair<uint64_t, uint64_t>> pieces;
+    const uint64_t ramp[3] = {std::max<uint64_t>(1, chunk / 8), std::max<uint64_t>(1, chunk / 4),
+                              std::max<uint64_t>(1, chunk / 2)};
+    const uint64_t ramp_total = ramp[0] + ramp[1] + ramp[2];
+    if (n < 2 * ramp_total + 2 * chunk) {  // short input: plain chunks
+        for (uint64_t off = 0; off < n; off += chunk) pieces.push_back({off, std::min(chunk, n - off)});
+        return pieces;
+    }
+    uint64_t off = 0;
+    for (uint64_t r : ramp) {
+        pieces.push_back({off, r});
+        off += r;
+    }
+    const uint64_t middle_end = n - ramp_total;
+    while (off < middle_end) {
+        const uint64_t len = std::min(chunk, middle_end - off);
+        pieces.push_back({off, len});
+        off += len;
+    }
+    for (int k = 2; k >= 0; --k) {
+        pieces.push_back({off, ramp[k]});
+        off += ramp[k];
+    }
+    return pieces;
+}
 
 struct PipelineStreams {
     cudaStream_t h2d = nullptr, d2h = nullptr;
@@ -64,10 +96,10 @@ heph_status scan_host_typed(Device *dev, int exclusive, const T *host_in, T *hos
     cudaEventDestroy(ready);
 
     heph_status st = HEPH_OK;
-    const uint64_t nchunks = (n + chunk - 1) / chunk;
-    for (uint64_t k = 0; k < nchunks && st == HEPH_OK; ++k) {
+    const auto pieces = pipeline_pieces(n, chunk);
+    for (uint64_t k = 0; k < pieces.size() && st == HEPH_OK; ++k) {
         const int s = (int)(k % slots);
-        const uint64_t off = k * chunk, len = std::min(chunk, n - off);
+        const uint64_t off = pieces[k].first, len = pieces[k].second;
         T *din = mem + (uint64_t)s * 2 * chunk, *dout = din + chunk;
         if (k >= slots) cudaStreamWaitEvent(ps.h2d, ps.drained[s], 0);  // slot's previous chunk is out
         if (cudaMemcpyAsync(din, host_in + off, len * sizeof(T), cudaMemcpyHostToDevice, ps.h2d) != cudaSuccess) {
