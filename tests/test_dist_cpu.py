@@ -1,5 +1,5 @@
-"""Host-side logic of the partitioned 1-D path with world_size 2 gloo ranks on
-CPU: each rank owns a contiguous slice, exchanges its slice total, derives its
+"""Host-side logic of the partitioned 1-D path with world_size 2-4 gloo ranks
+on CPU: each rank owns a contiguous slice, exchanges its slice total, derives its
 carry = fold of the lower ranks' totals (hephaestus_b200.dist.carries, the rule
 dist.cu applies on the device) and scans its slice seeded with it; the
 concatenation must equal the global scan.  A rank that fails before the
@@ -53,10 +53,9 @@ def _scan_worker(rank, world, port, exclusive, result_dir):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exclusive", [False, True])
-def test_partitioned_scan_rank_logic(tmp_path, exclusive):
+@pytest.mark.parametrize("exclusive,world", [(False, 2), (True, 2), (True, 3), (False, 4)])
+def test_partitioned_scan_rank_logic(tmp_path, exclusive, world):
     from oracle import host_ref as oracle
-    world = 2
     mp.spawn(_scan_worker, args=(world, _free_port(), exclusive, str(tmp_path)), nprocs=world, join=True)
     got = np.concatenate([np.load(tmp_path / f"r{r}.npy") for r in range(world)])
     full = oracle.generate(oracle.GEN_I32_PM1000, 4, 100_003)
