@@ -71,6 +71,9 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end measurement")
+    ap.add_argument("--misalign", type=int, default=0,
+                    help="configs 3/4: the same-shape view at element offset K of a row-padded matrix "
+                         "(rows not 16-byte aligned)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--n", type=int, default=None,
                     help="override the element count of configs 1, 2 and 5 (small profiling cases)")
@@ -270,6 +273,10 @@ def run_reference(args, cfg):
 def main():
     args = parse()
     cfg = dict(CONFIGS[args.config])
+    if args.misalign:
+        if args.config not in (3, 4):
+            raise SystemExit("--misalign applies to configs 3 and 4")
+        cfg["workload"] += f" [view at element offset {args.misalign} of a row-padded matrix: rows not 16-byte aligned]"
     if args.n is not None and "n" in cfg:
         cfg["n"] = int(args.n)
         cfg["workload"] += f" [reduced to {args.n} elements]"
@@ -369,13 +376,16 @@ def main():
         units = n * nbuf
     elif args.config == 3:
         rows, cols = cfg["rows"], cfg["cols"]
-        x = dev.alloc_uninitialized(np.float32, rows * cols)
+        k = args.misalign
+        ld = cols + k  # k > 0: every row starts at a different 16-byte misalignment
+        x = dev.alloc_uninitialized(np.float32, rows * ld + k)
         S.synth_fill(dev, x, S.SYNTH_F32_NORMAL, seed=2, stream=sp)
-        S.synth_inject_row_ties(dev, x, rows, cols, seed=2, stream=sp)
+        if k == 0:
+            S.synth_inject_row_ties(dev, x, rows, cols, seed=2, stream=sp)
         vals = dev.alloc_zeroed(np.float32, rows)
         idx = dev.alloc_zeroed(np.uint32, rows)
         ops = H.CudaAxisReductionOps()
-        il, ol = Layout.c_contiguous([rows, cols]), Layout.c_contiguous([rows, 1])
+        il, ol = Layout.try_new([rows, cols], [ld, 1], k), Layout.c_contiguous([rows, 1])
 
         def step():
             ops.argmax_axis_into(dev, StridedView(x, il), 1, StridedView(vals, ol), StridedView(idx, ol),
@@ -386,11 +396,13 @@ def main():
         units = rows * cols
     elif args.config == 4:
         rows, cols = cfg["rows"], cfg["cols"]
-        x = dev.alloc_uninitialized(np.float64, rows * cols)
+        k = args.misalign
+        ld = cols + (2 if k else 0)  # row stride stays a 16-byte multiple; the view starts k elements in
+        x = dev.alloc_uninitialized(np.float64, rows * ld + k)
         S.synth_fill(dev, x, S.SYNTH_F64_UNIT, seed=3, stream=sp)
         out = dev.alloc_zeroed(np.float64, cols)
         ops = H.CudaAxisReductionOps()
-        il, ol = Layout.c_contiguous([rows, cols]), Layout.c_contiguous([1, cols])
+        il, ol = Layout.try_new([rows, cols], [ld, 1], k), Layout.c_contiguous([1, cols])
 
         def step():
             ops.reduce_axis_into(SumOp, dev, StridedView(x, il), 0, StridedView(out, ol), stream=sp)

@@ -28,6 +28,7 @@ constexpr int kColThreads = 256;
 
 struct AxisArgs {
     int64_t in_base, in_o, in_r;
+    uint64_t lead;  // column kernel, vector form: columns before output 0 in its first 16-byte vector
     int64_t out_base, out_o;
     int64_t idx_base, idx_o;
     uint64_t outer, len;
@@ -71,9 +72,19 @@ __global__ void __launch_bounds__(kRowThreads)
 
     uint64_t r = r0;
     if constexpr (VEC) {
-        // r0 is a multiple of V and the row start is 16-byte aligned.
-        const uint64_t nv = (r1 - r0) / V;
-        const uint4 *vrow = reinterpret_cast<const uint4 *>(row + r0);
+        // Each (row, segment) aligns itself: a head of at most V - 1 elements
+        // (one per lane) up to the first 16-byte boundary, then 128-bit loads.
+        // Every lane still visits its indices in increasing order, which the
+        // arg-reductions' lowest-index tie-break relies on.
+        uint64_t head = ((16u - (reinterpret_cast<uintptr_t>(row + r0) & 15u)) & 15u) / sizeof(T);
+        if (head > r1 - r0) head = r1 - r0;
+        // The head element is loaded now and folded after the body, so its
+        // load does not hold back the vector loads.
+        const bool has_head = (uint64_t)lane < head;
+        const T hv = has_head ? row[r0 + lane] : T(0);
+        const uint64_t rv = r0 + head;
+        const uint64_t nv = (r1 - rv) / V;
+        const uint4 *vrow = reinterpret_cast<const uint4 *>(row + rv);
         uint64_t k = lane;
         for (; k + 32 * (U - 1) < nv; k += 32 * U) {
             uint4 raw[U];
@@ -83,15 +94,30 @@ __global__ void __launch_bounds__(kRowThreads)
             for (int u = 0; u < U; ++u) {
                 Vec16<T> e = as_elems<T>(raw[u]);
 #pragma unroll
-                for (int c = 0; c < V; ++c) take(e.e[c], r0 + (k + 32 * u) * V + c);
+                for (int c = 0; c < V; ++c) take(e.e[c], rv + (k + 32 * u) * V + c);
             }
         }
         for (; k < nv; k += 32) {
             Vec16<T> e = as_elems<T>(ld_stream(vrow + k));
 #pragma unroll
-            for (int c = 0; c < V; ++c) take(e.e[c], r0 + k * V + c);
+            for (int c = 0; c < V; ++c) take(e.e[c], rv + k * V + c);
         }
-        r = r0 + nv * V;
+        r = rv + nv * V;
+        for (uint64_t q = r + lane; q < r1; q += 32) take(row[q], q);
+        r = r1;
+        if (has_head) {
+            const uint32_t hi = (uint32_t)(r0 + lane);
+            if constexpr (ARG) {
+                // Folded out of index order: the index-aware comparison keeps
+                // the lowest index among equal extrema.
+                if (best == 0xffffffffu || arg_better<T, OP>(hv, hi, acc, best)) {
+                    acc = hv;
+                    best = hi;
+                }
+            } else {
+                acc = combine<T, OP>(acc, hv);
+            }
+        }
     }
     for (uint64_t q = r + lane; q < r1; q += 32) take(row[q], q);
 
@@ -148,8 +174,17 @@ __global__ void __launch_bounds__(kColThreads)
     constexpr int V = VEC ? Vec16<T>::V : 1;
     constexpr int U = 4;
     const uint64_t t = (uint64_t)blockIdx.x * kColThreads + threadIdx.x;
+    // Vector form: thread t covers the 16-byte vector of virtual columns
+    // [tV, tV + V); virtual column v is output v - lead.  The first and last
+    // vectors may hold columns outside the view: they are loaded (a 16-byte
+    // vector never leaves the page of the view element it holds) and masked.
+    const uint64_t lead = VEC ? a.lead : 0;
     const uint64_t o0 = t * V;
-    if (o0 >= a.outer) return;
+    if (o0 >= a.outer + lead) return;
+    uint32_t vmask = 0;
+#pragma unroll
+    for (int c = 0; c < V; ++c)
+        if (o0 + c >= lead && o0 + c < lead + a.outer) vmask |= 1u << c;
     const uint64_t s = blockIdx.y;
     const uint64_t r0 = s * a.seg;
     const uint64_t r1 = min(a.len, r0 + a.seg);
@@ -175,7 +210,8 @@ __global__ void __launch_bounds__(kColThreads)
     if constexpr (VEC) {
         // Full vector of V outputs (the launcher routes a ragged last vector
         // through the scalar instantiation).
-        const T *col = in + a.in_base + (int64_t)o0;
+        const T *col = in + a.in_base - (int64_t)lead + (int64_t)o0;
+        const bool all = vmask == (1u << V) - 1;
         uint64_t r = r0;
         for (; r + U <= r1; r += U) {
             uint4 raw[U];
@@ -186,14 +222,16 @@ __global__ void __launch_bounds__(kColThreads)
             for (int u = 0; u < U; ++u) {
                 Vec16<T> e = as_elems<T>(raw[u]);
 #pragma unroll
-                for (int c = 0; c < V; ++c) take(c, e.e[c], r + u);
+                for (int c = 0; c < V; ++c)
+                    if (all || ((vmask >> c) & 1u)) take(c, e.e[c], r + u);
             }
         }
         for (; r < r1; ++r) {
             Vec16<T> e =
                 as_elems<T>(ld_stream(reinterpret_cast<const uint4 *>(col + (int64_t)r * a.in_r)));
 #pragma unroll
-            for (int c = 0; c < V; ++c) take(c, e.e[c], r);
+            for (int c = 0; c < V; ++c)
+                if (all || ((vmask >> c) & 1u)) take(c, e.e[c], r);
         }
     } else {
         const T *col = in + a.in_base + (int64_t)o0 * a.in_o;
@@ -210,7 +248,8 @@ __global__ void __launch_bounds__(kColThreads)
 
 #pragma unroll
     for (int c = 0; c < V; ++c) {
-        const uint64_t o = o0 + c;
+        if (VEC && !((vmask >> c) & 1u)) continue;
+        const uint64_t o = o0 + c - lead;
         if (o >= a.outer) break;
         if (gridDim.y == 1) {
             T v = acc[c];
@@ -227,7 +266,6 @@ __global__ void __launch_bounds__(kColThreads)
 
 // ------------------------------------------------------------------ launch
 
-static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 template <typename T, int OP, bool ARG, bool MEAN>
 static heph_status launch_axis_typed(Device *dev, cudaStream_t stream, const T *in,
@@ -248,8 +286,10 @@ static heph_status launch_axis_typed(Device *dev, cudaStream_t stream, const T *
 
     if (p.in_r == 1) {
         // Row reduction: one warp per (row, segment).
-        const bool vec = aligned16(in + p.in_base) &&
-                         (p.outer == 1 || ((uint64_t)p.in_o * sizeof(T)) % 16 == 0);
+        // 128-bit loads whenever a row holds more than a few vectors: each
+        // (row, segment) aligns its own start, so misaligned rows (odd column
+        // offsets, odd leading dimensions) stream at full width too.
+        const bool vec = p.len >= 4 * V;
         const uint64_t warps_wanted = resident_threads / 32 * 2;
         uint64_t splits = 1;
         if (p.outer < warps_wanted && p.len >= 8192) {
@@ -290,18 +330,21 @@ static heph_status launch_axis_typed(Device *dev, cudaStream_t stream, const T *
     }
 
     // Column reduction: thread per output (vector of V outputs when the
-    // outputs are adjacent in memory and rows are 16-byte aligned).
-    const bool vec_ok = p.in_o == 1 && aligned16(in + p.in_base) &&
+    // outputs are adjacent in memory and the row stride is a multiple of 16
+    // bytes).  A view starting off a 16-byte boundary (an odd column offset)
+    // runs its first few columns scalar and vectorises the rest.
+    const bool vec_ok = p.in_o == 1 && p.outer >= (uint64_t)V &&
                         (p.len <= 1 || ((uint64_t)p.in_r * sizeof(T)) % 16 == 0);
-    const uint64_t full_vec_outputs = vec_ok ? (p.outer / V) * V : 0;
+    const uint64_t lead = vec_ok ? (reinterpret_cast<uintptr_t>(in + p.in_base) & 15u) / sizeof(T) : 0;
+    a.lead = lead;
     std::lock_guard<std::mutex> lock(dev->mu);
-    // Two launches at most: the vectorised body and a scalar ragged edge.
+    // One launch: vectors over all outputs (edge vectors masked), or scalar.
     struct Part {
         uint64_t o_begin, o_count;
         bool vec;
-    } parts[2] = {{0, full_vec_outputs, true}, {full_vec_outputs, p.outer - full_vec_outputs, false}};
+    } parts[1] = {{0, p.outer, vec_ok}};
     // Row slices: enough CTAs for two waves, slices of at least 64 rows.
-    const uint64_t threads_x = full_vec_outputs / V + (p.outer - full_vec_outputs);
+    const uint64_t threads_x = vec_ok ? (lead + p.outer + V - 1) / V : p.outer;
     const uint64_t blocks_x_total = (threads_x + kColThreads - 1) / kColThreads;
     const uint64_t cta_wanted = (uint64_t)dev->sm_count * (2048 / kColThreads) * 2;
     uint64_t splits = 1;
@@ -329,8 +372,7 @@ static heph_status launch_axis_typed(Device *dev, cudaStream_t stream, const T *
         b.out_base = a.out_base + (int64_t)part.o_begin * a.out_o;
         b.idx_base = a.idx_base + (int64_t)part.o_begin * a.idx_o;
         b.outer = part.o_count;
-        const uint64_t per_thread = part.vec ? V : 1;
-        const uint64_t tx = (part.o_count + per_thread - 1) / per_thread;
+        const uint64_t tx = part.vec ? threads_x : part.o_count;
         dim3 grid((unsigned)((tx + kColThreads - 1) / kColThreads), (unsigned)splits);
         // Partials of this part are written at [s * outer_part + o]; give each
         // part its own region so the finalize below can address them.

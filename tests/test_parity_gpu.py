@@ -607,3 +607,54 @@ def test_fused_batch_widening_and_hazards(device, oracle):
     S.Batch(device, [it1, it2, it3]).launch()
     assert device.download_owned(t)[0] == 5050 + 7
     assert list(device.download_owned(b)) == [7, 7]
+
+
+# Axis reductions over views whose rows do not start on a 16-byte boundary
+# (odd column offsets, odd leading dimensions): rows align themselves per
+# (row, segment), column reductions run a scalar head before the vector body.
+MISALIGNED_AXIS_VIEWS = [
+    Layout.try_new([17, 8000], [8003, 1], 1),     # odd leading dimension
+    Layout.try_new([5, 20000], [20001, 1], 3),    # few long rows: split into segments
+    Layout.try_new([300, 257], [260, 1], 1),      # row stride 16-byte multiple, odd offset
+    Layout.try_new([100, 1000], [1004, 1], 2),
+    Layout.try_new([64, 131], [131, 1], 5),       # dense rows of odd length at an odd offset
+]
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_misaligned_axis_reductions(device, oracle, dt):
+    rng = np.random.default_rng(23)
+    ops = CudaAxisReductionOps()
+    x = rand(dt, 150_000, rng)
+    buf = device.upload(x)
+    for lay in MISALIGNED_AXIS_VIEWS:
+        for axis in (0, 1):
+            for op in (0, 2, 3):
+                oshape = list(lay.shape)
+                oshape[axis] = 1
+                out = device.alloc_zeroed(dt, oshape[0] * oshape[1])
+                ops.reduce_axis_into(OPS[op], device, StridedView(buf, lay), axis,
+                                     StridedView(out, Layout.c_contiguous(oshape)))
+                want = oracle.reduce_axis(x, lay.shape, axis, op=op, in_strides=lay.strides, in_offset=lay.offset)
+                assert_close(device.download_owned(out), want, dt, x)
+
+
+@pytest.mark.parametrize("dt", [np.float32, np.int32, np.float64])
+@pytest.mark.parametrize("op", [3, 2])
+def test_misaligned_arg_reductions_with_ties(device, oracle, dt, op):
+    rng = np.random.default_rng(29 + op)
+    ops = CudaAxisReductionOps()
+    x = rng.integers(0, 7, size=150_000).astype(dt)  # few distinct values: many exact ties
+    buf = device.upload(x)
+    fn = ops.argmax_axis_into if op == 3 else ops.argmin_axis_into
+    for lay in MISALIGNED_AXIS_VIEWS:
+        for axis in (0, 1):
+            oshape = list(lay.shape)
+            oshape[axis] = 1
+            n = oshape[0] * oshape[1]
+            vals, idx = device.alloc_zeroed(dt, n), device.alloc_zeroed(np.uint32, n)
+            ol = Layout.c_contiguous(oshape)
+            fn(device, StridedView(buf, lay), axis, StridedView(vals, ol), StridedView(idx, ol))
+            wv, wi = oracle.arg_reduce_axis(x, lay.shape, axis, op=op, in_strides=lay.strides, in_offset=lay.offset)
+            np.testing.assert_array_equal(device.download_owned(idx), wi, err_msg=str(lay))
+            np.testing.assert_array_equal(device.download_owned(vals), wv)
