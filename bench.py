@@ -3,9 +3,12 @@ GB/s for reduce/scan).
 
 Default workload: u32 exclusive prefix scan over
 2^28 elements per GPU, values h & 15 from seed 1 (SplitMix64 stream, generated
-on the device).  At N>1 GPUs every rank owns 2^28 elements of one global
-N*2^28-element buffer (weak scaling) and the step is the partitioned scan:
-local total -> NCCL all-gather of the totals -> carry -> seeded look-back scan.
+on the device).  At N>1 GPUs config 2 runs as replicas (every rank scans its own
+2^28 elements, weak scaling); with --partitioned every rank owns 2^28 elements of
+one global N*2^28-element buffer and the step is the partitioned scan: local total
+-> NCCL all-gather of the totals -> carry -> seeded scan.  Config 5 is the 1-D
+partitioned case: 2^32 i32 split over the ranks (strong scaling), its scan and
+i64 sum fused so that one pass over each slice feeds both exchanges.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
                   [--config 1|2|3|4|5|6|7]
@@ -71,6 +74,8 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end measurement")
+    ap.add_argument("--partitioned", action="store_true",
+                    help="config 2 at N>1: one global scan partitioned over the ranks instead of replicas")
     ap.add_argument("--misalign", type=int, default=0,
                     help="configs 3/4: the same-shape view at element offset K of a row-padded matrix "
                          "(rows not 16-byte aligned)")
@@ -321,7 +326,10 @@ def main():
         return float(t.item())
 
     comm = None
-    if world > 1 and args.config in (2, 5):
+    # Config 2 runs as replicas at N>1 (every rank scans its own 2^28
+    # elements; the 1-D partitioned case is config 5); --partitioned makes it
+    # one global scan over all ranks' slices instead.
+    if world > 1 and (args.config == 5 or (args.config == 2 and args.partitioned)):
         from hephaestus_b200.dist import Communicator
         comm = Communicator.from_torch(dev)
 
@@ -331,7 +339,7 @@ def main():
     if args.config == 2:
         n = cfg["n"]
         x = dev.alloc_uninitialized(np.uint32, n)
-        S.synth_fill(dev, x, S.SYNTH_U32_LOW4, seed=1, index_base=rank * n, stream=sp)
+        S.synth_fill(dev, x, S.SYNTH_U32_LOW4, seed=1, index_base=rank * n if comm else 0, stream=sp)
         y = dev.alloc_uninitialized(np.uint32, n)
         lay = Layout.c_contiguous([n])
         bytes_per_step = 8 * n
@@ -438,10 +446,12 @@ def main():
         lay = Layout.c_contiguous([n])
         one = Layout.c_contiguous([1])
         if comm:
+            # One pass over the slice yields both the scan's carry total and
+            # the sum's partial; one all-gather exchanges both.
             def step():
-                comm.scan_into(CumSumOp, StridedView(x, lay), StridedView(y, lay), stream=sp)
-                comm.reduce_full_into(SumOp, StridedView(x, lay), StridedView(s64, one), stream=sp)
-            launches_per_step = 7
+                comm.scan_reduce_into(CumSumOp, StridedView(x, lay), StridedView(y, lay), SumOp,
+                                      StridedView(s64, one), stream=sp)
+            launches_per_step = 3  # dual reduction, rank fold, scan (+ the NCCL all-gather)
         else:
             sops, fops = H.CudaScanOps(), H.CudaFullReductionOps()
 

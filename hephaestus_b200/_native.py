@@ -107,6 +107,7 @@ SIGNATURES = [
     ("heph_comm_abort", _st, [_vp]),
     ("heph_partitioned_reduce_full", _st, [_vp, _i, _vp, _lp, _vp, _lp, _vp]),
     ("heph_partitioned_scan", _st, [_vp, _i, _i, _vp, _lp, _vp, _lp, _vp]),
+    ("heph_partitioned_scan_reduce", _st, [_vp, _i, _i, _vp, _lp, _vp, _lp, _i, _vp, _lp, _vp]),
     ("heph_scan_seeded", _st, [_vp, _i, _i, _vp, _lp, _vp, _lp, _vp, _u64, _vp]),
     ("heph_scan_host", _st, [_vp, _i, _i, _i, _vp, _vp, _u64, _u64]),
     ("heph_reduce_full_noalloc", _st, [_i, _i, _i, _vp, _u64, _vp, _vp]),

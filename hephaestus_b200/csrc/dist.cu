@@ -10,6 +10,12 @@
 //   scan:   local reduction of the slice (its total) -> ncclAllGather of the
 //           totals -> carry = fold of the lower ranks' totals -> look-back
 //           scan of the slice seeded with the carry.
+//   scan + reduce of the same slice (heph_partitioned_scan_reduce): ONE
+//           local pass computes the slice's scan total and its reduction
+//           partial, one ncclAllGather carries both (16 bytes per rank), one
+//           thread folds the carry and the global reduction, then the seeded
+//           scan: every rank moves 3 bytes-units per element, as one GPU does
+//           for the same pair, so the pair scales with the rank count.
 // NCCL is resolved at run time from the libnccl.so.2 already loaded into the
 // process (torch's), else from the loader path, so this library carries no
 // link-time NCCL dependency.
@@ -93,6 +99,40 @@ heph_status launch_fold(cudaStream_t s, int op, const void *g, int count, void *
     return HEPH_OK;
 }
 
+// carry = op1-fold of the totals of ranks < rank; global = op2-fold of every
+// rank's partial; pairs are [T total | pad][Tacc partial | pad], 16 bytes each.
+template <typename T, int OP1, typename Tacc, int OP2>
+__global__ void fold_pairs_kernel(const unsigned char *__restrict__ pairs, int nranks, int rank, T *__restrict__ carry,
+                                  Tacc *__restrict__ global) {
+    T c = identity<T, OP1>();
+    Tacc g = identity<Tacc, OP2>();
+    for (int r = 0; r < nranks; ++r) {
+        const T t = *reinterpret_cast<const T *>(pairs + 16 * r);
+        const Tacc v = *reinterpret_cast<const Tacc *>(pairs + 16 * r + 8);
+        if (r < rank) c = combine<T, OP1>(c, t);
+        g = combine<Tacc, OP2>(g, v);
+    }
+    *carry = c;
+    *global = g;
+}
+
+template <typename T, int OP1, typename Tacc>
+heph_status launch_fold_pairs(cudaStream_t s, int op2, const void *pairs, int nranks, int rank, void *carry,
+                              void *global) {
+    const unsigned char *pp = static_cast<const unsigned char *>(pairs);
+    T *c = static_cast<T *>(carry);
+    Tacc *g = static_cast<Tacc *>(global);
+    switch (op2) {
+        case OP_SUM: fold_pairs_kernel<T, OP1, Tacc, OP_SUM><<<1, 1, 0, s>>>(pp, nranks, rank, c, g); break;
+        case OP_PROD: fold_pairs_kernel<T, OP1, Tacc, OP_PROD><<<1, 1, 0, s>>>(pp, nranks, rank, c, g); break;
+        case OP_MIN: fold_pairs_kernel<T, OP1, Tacc, OP_MIN><<<1, 1, 0, s>>>(pp, nranks, rank, c, g); break;
+        case OP_MAX: fold_pairs_kernel<T, OP1, Tacc, OP_MAX><<<1, 1, 0, s>>>(pp, nranks, rank, c, g); break;
+        default: return fail(HEPH_INVALID_CONFIGURATION, "full reduction supports sum, prod, min and max");
+    }
+    HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "rank fold launch");
+    return HEPH_OK;
+}
+
 }  // namespace
 }  // namespace heph
 
@@ -102,7 +142,10 @@ struct heph_comm {
     Device *device = nullptr;
     ncclComm_t nccl = nullptr;
     int nranks = 0, rank = 0;
-    void *scratch = nullptr;  // [total: 8 B][carry: 8 B][gathered: 8 B x nranks]
+    // [total: 8 B][carry: 8 B][gathered: 8 B x nranks] then, from pair_off:
+    // [pair: 16 B][carry: 16 B][gathered pairs: 16 B x nranks]
+    void *scratch = nullptr;
+    size_t pair_off = 0;
     bool aborted = false;
 };
 
@@ -140,7 +183,8 @@ extern "C" heph_status heph_comm_init(heph_device *device, const uint8_t id[HEPH
         delete c;
         return nccl_fail(r, "ncclCommInitRank");
     }
-    if (cudaMalloc(&c->scratch, 16 + 8 * (size_t)nranks) != cudaSuccess) {
+    c->pair_off = (16 + 8 * (size_t)nranks + 15) & ~size_t(15);
+    if (cudaMalloc(&c->scratch, c->pair_off + 32 + 16 * (size_t)nranks) != cudaSuccess) {
         cudaGetLastError();
         api.CommDestroy(c->nccl);
         delete c;
@@ -249,4 +293,72 @@ extern "C" heph_status heph_partitioned_scan(heph_comm *comm, heph_op op, int ex
     if (noop) return HEPH_OK;
     // 4. single-pass scan of the slice seeded with the carry.
     return launch_scan(dev, s, op, bi->dtype, bi->ptr, bo->ptr, p, false, exclusive != 0, scratch + 8);
+}
+
+extern "C" heph_status heph_partitioned_scan_reduce(heph_comm *comm, heph_op scan_op, int exclusive,
+                                                    const heph_buffer *in, const heph_layout *in_layout,
+                                                    heph_buffer *scan_out, const heph_layout *scan_layout,
+                                                    heph_op reduce_op, heph_buffer *reduce_out,
+                                                    const heph_layout *reduce_layout, heph_stream stream) {
+    heph_status st = partitioned_args(comm, in, in_layout, scan_out, scan_layout);
+    if (st != HEPH_OK) return st;
+    if (!reduce_out || !reduce_layout) return fail(HEPH_INVALID_CONFIGURATION, "null argument");
+    const Buffer *bi = reinterpret_cast<const Buffer *>(in);
+    Buffer *bo = reinterpret_cast<Buffer *>(scan_out);
+    Buffer *br = reinterpret_cast<Buffer *>(reduce_out);
+    if (br->device != comm->device) return fail(HEPH_DISPATCH_FAILED, "operand buffers belong to another device");
+    if (scan_op != HEPH_SUM && scan_op != HEPH_PROD)
+        return fail(HEPH_INVALID_CONFIGURATION, "scans support the sum (cumsum) and product (cumprod) operators");
+    if (reduce_op != HEPH_SUM && reduce_op != HEPH_PROD && reduce_op != HEPH_MIN && reduce_op != HEPH_MAX)
+        return fail(HEPH_INVALID_CONFIGURATION, "full reduction supports sum, prod, min and max");
+    if (bi->dtype != bo->dtype) return fail(HEPH_DISPATCH_FAILED, "scan output element type must match the input");
+    const bool widen = (bi->dtype == HEPH_I32 && br->dtype == HEPH_I64) ||
+                       (bi->dtype == HEPH_F32 && br->dtype == HEPH_F64);
+    if (bi->dtype != br->dtype && !widen)
+        return fail(HEPH_DISPATCH_FAILED, "full reduction output element type must match the input or widen it");
+    uint64_t count = 0;
+    st = plan_full_reduction(*in_layout, bi->len, *reduce_layout, br->len, &count);
+    if (st != HEPH_OK) return st;
+    bool noop = false;
+    AxisProblem p;
+    st = plan_axis_scan(*in_layout, bi->len, *scan_layout, bo->len, 0, bi->ptr == bo->ptr, &noop, &p);
+    if (st != HEPH_OK) return st;
+    Device *dev = comm->device;
+    st = bind(dev);
+    if (st != HEPH_OK) return st;
+    cudaStream_t s = resolve_stream(dev, stream);
+    char *pair = static_cast<char *>(comm->scratch) + comm->pair_off;
+    char *carry = pair + 16, *gathered = pair + 32;
+    // 1. the slice's scan total and reduction partial in one read (two reads
+    //    when the slice is not one dense run).
+    const int64_t first = (int64_t)in_layout->offset;
+    if (count > 0 && layout_is_dense(*in_layout)) {
+        const void *base = static_cast<const char *>(bi->ptr) + first * (int64_t)dtype_size(bi->dtype);
+        st = launch_reduce_dual(dev, s, scan_op, reduce_op, bi->dtype, br->dtype, base, count, pair, pair + 8);
+    } else {
+        st = launch_reduce_full(dev, s, scan_op, bi->dtype, bi->dtype, bi->ptr, *in_layout, count, pair);
+        if (st == HEPH_OK)
+            st = launch_reduce_full(dev, s, reduce_op, bi->dtype, br->dtype, bi->ptr, *in_layout, count, pair + 8);
+    }
+    if (st != HEPH_OK) return st;
+    // 2. every rank's pair.
+    ncclResult_t r = nccl().AllGather(pair, gathered, 16, ncclUint8, comm->nccl, s);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
+    // 3. carry (lower ranks' totals) and the global reduction (all partials).
+    void *gdst = static_cast<char *>(br->ptr) + reduce_layout->offset * dtype_size(br->dtype);
+    auto fold = [&]<typename T, typename Tacc>() -> heph_status {
+        if (scan_op == HEPH_SUM)
+            return launch_fold_pairs<T, OP_SUM, Tacc>(s, reduce_op, gathered, comm->nranks, comm->rank, carry, gdst);
+        return launch_fold_pairs<T, OP_PROD, Tacc>(s, reduce_op, gathered, comm->nranks, comm->rank, carry, gdst);
+    };
+    if (bi->dtype == br->dtype)
+        st = dispatch_dtype(bi->dtype, [&]<typename T>() { return fold.template operator()<T, T>(); });
+    else if (bi->dtype == HEPH_I32)
+        st = fold.template operator()<int32_t, int64_t>();
+    else
+        st = fold.template operator()<float, double>();
+    if (st != HEPH_OK) return st;
+    if (noop) return HEPH_OK;
+    // 4. the slice's scan seeded with the carry.
+    return launch_scan(dev, s, scan_op, bi->dtype, bi->ptr, bo->ptr, p, false, exclusive != 0, carry);
 }

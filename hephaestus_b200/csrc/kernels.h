@@ -38,6 +38,12 @@ heph_status launch_reduce_full_fused(cudaStream_t stream, int op, heph_dtype in_
                                      const FusedFull *table, uint32_t nprob, uint32_t grid, void *partials,
                                      unsigned int *tickets);
 
+// Two reductions of one dense run of n elements in one read: op1 in the
+// input type into out1, op2 in acc2_dtype (the input type or its widening)
+// into out2.
+heph_status launch_reduce_dual(Device *dev, cudaStream_t stream, int op1, int op2, heph_dtype dtype,
+                               heph_dtype acc2_dtype, const void *in, uint64_t n, void *out1, void *out2);
+
 // Rank-2 axis reduction.  `mean` divides the sum by the axis length;
 // `indices` (u32, same layout as out) selects the arg-reduction form.
 heph_status launch_reduce_axis(Device *dev, cudaStream_t stream, int op, heph_dtype dtype,

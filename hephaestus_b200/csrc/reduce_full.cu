@@ -340,6 +340,125 @@ heph_status launch_reduce_full(Device *dev, cudaStream_t stream, int op, heph_dt
                 "f32->f64)");
 }
 
+// Two reductions of one dense run in one read: op1 in T (e.g. the total a
+// partitioned scan needs for its carry) and op2 in Tacc (e.g. a widening sum
+// of the same slice).  Per-CTA partials of both, last-CTA finalize of both.
+template <typename Tin, int OP1, typename Tacc, int OP2>
+__global__ void __launch_bounds__(kReduceThreads)
+    reduce_dual_kernel(const Tin *__restrict__ in, uint64_t n, Tin *__restrict__ out1, Tacc *__restrict__ out2,
+                       Tin *__restrict__ partials1, Tacc *__restrict__ partials2, unsigned int *__restrict__ ticket) {
+    __shared__ Tin scratch1[kReduceThreads / 32];
+    __shared__ Tacc scratch2[kReduceThreads / 32];
+    constexpr int V = Vec16<Tin>::V;
+    const uint64_t tid = (uint64_t)blockIdx.x * kReduceThreads + threadIdx.x;
+    const uint64_t stride = (uint64_t)gridDim.x * kReduceThreads;
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(in);
+    uint64_t head = ((16u - (addr & 15u)) & 15u) / sizeof(Tin);
+    if (head > n) head = n;
+    const uint64_t nvec = (n - head) / V;
+    const uint64_t tail = head + nvec * V;
+    const uint4 *vin = reinterpret_cast<const uint4 *>(in + head);
+    Tin a1 = identity<Tin, OP1>();
+    Tacc a2 = identity<Tacc, OP2>();
+    auto fold = [&](uint4 raw) {
+        Vec16<Tin> e = as_elems<Tin>(raw);
+#pragma unroll
+        for (int c = 0; c < V; ++c) {
+            a1 = combine<Tin, OP1>(a1, e.e[c]);
+            a2 = combine<Tacc, OP2>(a2, (Tacc)e.e[c]);
+        }
+    };
+    uint64_t i = tid;
+    for (; i + (kReduceUnroll - 1) * stride < nvec; i += kReduceUnroll * stride) {
+        uint4 r[kReduceUnroll];
+#pragma unroll
+        for (int u = 0; u < kReduceUnroll; ++u) r[u] = ld_stream(vin + i + u * stride);
+#pragma unroll
+        for (int u = 0; u < kReduceUnroll; ++u) fold(r[u]);
+    }
+    for (; i < nvec; i += stride) fold(ld_stream(vin + i));
+    auto fold_one = [&](Tin v) {
+        a1 = combine<Tin, OP1>(a1, v);
+        a2 = combine<Tacc, OP2>(a2, (Tacc)v);
+    };
+    if (tid < head) fold_one(in[tid]);
+    if (tid < n - tail) fold_one(in[tail + tid]);
+
+    a1 = block_fold<Tin, OP1, kReduceThreads>(a1, scratch1);
+    a2 = block_fold<Tacc, OP2, kReduceThreads>(a2, scratch2);
+    if (gridDim.x == 1) {
+        if (threadIdx.x == 0) {
+            *out1 = a1;
+            *out2 = a2;
+        }
+        return;
+    }
+    __shared__ bool am_last;
+    if (threadIdx.x == 0) {
+        partials1[blockIdx.x] = a1;
+        partials2[blockIdx.x] = a2;
+        __threadfence();
+        am_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!am_last) return;
+    __threadfence();
+    Tin b1 = identity<Tin, OP1>();
+    Tacc b2 = identity<Tacc, OP2>();
+    for (unsigned int j = threadIdx.x; j < gridDim.x; j += kReduceThreads) {
+        b1 = combine<Tin, OP1>(b1, ld_cg(partials1 + j));
+        b2 = combine<Tacc, OP2>(b2, ld_cg(partials2 + j));
+    }
+    b1 = block_fold<Tin, OP1, kReduceThreads>(b1, scratch1);
+    b2 = block_fold<Tacc, OP2, kReduceThreads>(b2, scratch2);
+    if (threadIdx.x == 0) {
+        *out1 = b1;
+        *out2 = b2;
+        *ticket = 0u;
+    }
+}
+
+template <typename Tin, int OP1, typename Tacc>
+static heph_status launch_dual_typed(Device *dev, cudaStream_t stream, int op2, const Tin *in, uint64_t n,
+                                     void *out1, void *out2) {
+    const uint64_t per_cta = (uint64_t)kReduceThreads * kReduceUnroll * (16 / sizeof(Tin));
+    const uint64_t cap = (uint64_t)dev->sm_count * (2048 / kReduceThreads);
+    const unsigned grid = (unsigned)std::max<uint64_t>(1, std::min((n + per_cta - 1) / per_cta, cap));
+    std::lock_guard<std::mutex> lock(dev->mu);
+    Workspace *ws = nullptr;
+    heph_status st = workspace_for(dev, stream, (size_t)grid * (sizeof(Tin) + sizeof(Tacc)) + 16, 0, &ws);
+    if (st != HEPH_OK) return st;
+    Tacc *p2 = static_cast<Tacc *>(ws->partials);
+    Tin *p1 = reinterpret_cast<Tin *>(static_cast<char *>(ws->partials) + (size_t)grid * sizeof(Tacc));
+    Tin *o1 = static_cast<Tin *>(out1);
+    Tacc *o2 = static_cast<Tacc *>(out2);
+    switch (op2) {
+        case OP_SUM: reduce_dual_kernel<Tin, OP1, Tacc, OP_SUM><<<grid, kReduceThreads, 0, stream>>>(in, n, o1, o2, p1, p2, ws->tickets); break;
+        case OP_PROD: reduce_dual_kernel<Tin, OP1, Tacc, OP_PROD><<<grid, kReduceThreads, 0, stream>>>(in, n, o1, o2, p1, p2, ws->tickets); break;
+        case OP_MIN: reduce_dual_kernel<Tin, OP1, Tacc, OP_MIN><<<grid, kReduceThreads, 0, stream>>>(in, n, o1, o2, p1, p2, ws->tickets); break;
+        case OP_MAX: reduce_dual_kernel<Tin, OP1, Tacc, OP_MAX><<<grid, kReduceThreads, 0, stream>>>(in, n, o1, o2, p1, p2, ws->tickets); break;
+        default: return fail(HEPH_INVALID_CONFIGURATION, "full reduction supports sum, prod, min and max");
+    }
+    HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "dual reduction launch");
+    return HEPH_OK;
+}
+
+heph_status launch_reduce_dual(Device *dev, cudaStream_t stream, int op1, int op2, heph_dtype dtype,
+                               heph_dtype acc2_dtype, const void *in, uint64_t n, void *out1, void *out2) {
+    auto by_op1 = [&]<typename Tin, typename Tacc>() -> heph_status {
+        const Tin *ti = static_cast<const Tin *>(in);
+        if (op1 == OP_SUM) return launch_dual_typed<Tin, OP_SUM, Tacc>(dev, stream, op2, ti, n, out1, out2);
+        if (op1 == OP_PROD) return launch_dual_typed<Tin, OP_PROD, Tacc>(dev, stream, op2, ti, n, out1, out2);
+        return fail(HEPH_INVALID_CONFIGURATION, "scans support the sum (cumsum) and product (cumprod) operators");
+    };
+    if (dtype == acc2_dtype)
+        return dispatch_dtype(dtype, [&]<typename T>() { return by_op1.template operator()<T, T>(); });
+    if (dtype == HEPH_I32 && acc2_dtype == HEPH_I64) return by_op1.template operator()<int32_t, int64_t>();
+    if (dtype == HEPH_F32 && acc2_dtype == HEPH_F64) return by_op1.template operator()<float, double>();
+    return fail(HEPH_DISPATCH_FAILED,
+                "full reduction output element type must match the input or widen it (i32->i64, f32->f64)");
+}
+
 uint32_t plan_reduce_full_fused(const Device *dev, heph_dtype in_dtype, FusedFull *table, uint32_t nprob) {
     const uint64_t per_cta = (uint64_t)kReduceThreads * kReduceUnroll * (16 / dtype_size(in_dtype));
     const uint64_t cap = (uint64_t)dev->sm_count * (2048 / kReduceThreads);

@@ -57,6 +57,17 @@ class Communicator:
                                           output.buffer.handle, ctypes.byref(ol),
                                           ctypes.c_void_p(stream) if stream else None))
 
+    def scan_reduce_into(self, scan_op, input: StridedView, scan_output: StridedView, reduce_op,
+                         reduce_output: StridedView, exclusive: bool = False, stream=None):
+        """scan_into and reduce_full_into of the same global buffer in one pass
+        over the slice for both exchanges (heph_partitioned_scan_reduce)."""
+        il, sl, rl = input.layout.native(), scan_output.layout.native(), reduce_output.layout.native()
+        check(N.lib.heph_partitioned_scan_reduce(self._h, scan_op.code, int(bool(exclusive)),
+                                                 input.buffer.handle, ctypes.byref(il),
+                                                 scan_output.buffer.handle, ctypes.byref(sl), reduce_op.code,
+                                                 reduce_output.buffer.handle, ctypes.byref(rl),
+                                                 ctypes.c_void_p(stream) if stream else None))
+
     def abort(self):
         if self._h:
             N.lib.heph_comm_abort(self._h)

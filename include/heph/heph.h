@@ -365,6 +365,19 @@ heph_status heph_partitioned_scan(heph_comm *comm, heph_op op, int exclusive,
                                   const heph_buffer *in, const heph_layout *in_layout,
                                   heph_buffer *out, const heph_layout *out_layout,
                                   heph_stream stream);
+/* heph_partitioned_scan and heph_partitioned_reduce_full of the SAME global
+ * buffer in one call (no counterpart in the reference): one local pass
+ * computes the slice's scan total (scan_op: SUM, PROD) and its reduction
+ * partial (reduce_op: SUM, PROD, MIN, MAX; reduce_out may widen I32->I64 /
+ * F32->F64), one all-gather carries both, then the seeded scan.  Each rank
+ * reads its slice twice and writes it once - the traffic of the same pair of
+ * calls on one GPU - instead of three reads.  Outputs must not alias the
+ * input. */
+heph_status heph_partitioned_scan_reduce(heph_comm *comm, heph_op scan_op, int exclusive,
+                                         const heph_buffer *in, const heph_layout *in_layout,
+                                         heph_buffer *scan_out, const heph_layout *scan_layout,
+                                         heph_op reduce_op, heph_buffer *reduce_out,
+                                         const heph_layout *reduce_layout, heph_stream stream);
 
 /* ------------------------------------------ [EXT] seeded scan building block */
 

@@ -31,6 +31,10 @@ def test_partitioned_scan_and_reduce(tmp_path, oracle):
     np.testing.assert_array_equal(xu, oracle.generate(oracle.GEN_U32_LOW4, 1, xu.size))
     np.testing.assert_array_equal(cat("scan_i32"), oracle.scan_axis(xi, [xi.size], 0))
     np.testing.assert_array_equal(cat("scan_u32"), oracle.scan_axis(xu, [xu.size], 0, exclusive=True))
+    np.testing.assert_array_equal(cat("fscan_i32"), oracle.scan_axis(xi, [xi.size], 0))
+    np.testing.assert_array_equal(cat("fscan_u32"), oracle.scan_axis(xu, [xu.size], 0, exclusive=True))
     for r in range(world):
         assert np.load(tmp_path / f"sum_{r}.npy")[0] == int(xi.astype(np.int64).sum())
         assert np.load(tmp_path / f"max_{r}.npy")[0] == xu.max()
+        assert np.load(tmp_path / f"fsum_{r}.npy")[0] == int(xi.astype(np.int64).sum())
+        assert np.load(tmp_path / f"fmax_{r}.npy")[0] == xu.max()
