@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end measurement")
+    ap.add_argument("--published", action="store_true",
+                    help="time the reference's own published reduce/scan cases (benchmark_results.md) instead")
     ap.add_argument("--partitioned", action="store_true",
                     help="config 2 at N>1: one global scan partitioned over the ranks instead of replicas")
     ap.add_argument("--misalign", type=int, default=0,
@@ -275,8 +277,111 @@ def run_reference(args, cfg):
 # --------------------------------------------------------------------- b200 arm
 
 
+# The reference's published reduce/scan/map cases (benchmark_results.md:151-181,
+# WGPU on a GeForce RTX 5080): name, its GPU time in us.
+PUBLISHED = [
+    ("sum f32 N=2^20 (prepared)", 42.70),
+    ("axis-0 sum 256x256 f32 (prepared)", 22.14),
+    ("axis-0 min 256x256 f32 (prepared)", 20.73),
+    ("axis-0 max 256x256 f32 (prepared)", 11.78),
+    ("axis-0 mean 256x256 f32 (prepared)", 18.05),
+    ("cumsum 256x256 f32 axis 1", 46.53),
+    ("dot f32 N=65536", 97.42),
+    ("trace 256x256 f32", 42.72),
+    ("norm L1 f32 N=65536", 78.14),
+    ("norm L2 f32 N=65536", 162.24),
+    ("norm max f32 N=65536", 89.88),
+]
+
+
+def run_published(args):
+    """Times the reference's published small cases through this library on
+    one B200: device_us = CUDA-event time of one call queued behind a short
+    spin (the events bracket the device work, not the host's issue time);
+    host_us = wall time of one call + synchronisation (+ the 1-element
+    read-back for the cases that return a scalar), Python/ctypes included."""
+    import torch
+    sys.path.insert(0, ROOT)
+    import hephaestus_b200 as H
+    import hephaestus_b200.seams as S
+    from hephaestus_b200.core import CumSumOp, Layout, MaxOp, MinOp, StridedView, SumOp
+    from hephaestus_b200 import _native as N
+
+    dev = H.CudaDevice(0)
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+    rng = np.random.default_rng(0)
+    one = Layout.c_contiguous([1])
+
+    def up(shape):
+        return dev.upload(rng.uniform(-1, 1, size=int(np.prod(shape))).astype(np.float32))
+
+    v20, m256, v64k, w64k = up([1 << 20]), up([256, 256]), up([65536]), up([65536])
+    out1 = dev.alloc_zeroed(np.float32, 1)
+    row = dev.alloc_zeroed(np.float32, 256)
+    scanned = dev.alloc_zeroed(np.float32, 256 * 256)
+    fops, aops, sops = H.CudaFullReductionOps(), H.CudaAxisReductionOps(), H.CudaScanOps()
+    ml, rl = Layout.c_contiguous([256, 256]), Layout.c_contiguous([1, 256])
+    p_sum = fops.prepare_reduce_full(SumOp, dev, StridedView(v20, Layout.c_contiguous([1 << 20])), StridedView(out1, one))
+    p_axis = {name: aops.prepare_reduce_axis_into(op, dev, StridedView(m256, ml), 0, StridedView(row, rl))
+              for name, op in (("sum", SumOp), ("min", MinOp), ("max", MaxOp))}
+    p_mean = S.prepare_mean_axis_into(dev, StridedView(m256, ml), 0, StridedView(row, rl))
+    p_scan = sops.prepare_scan_axis(CumSumOp, dev, StridedView(m256, ml), 1, N.FORWARD, StridedView(scanned, ml))
+    p_dot = S.prepare_dot(dev, StridedView(v64k, Layout.c_contiguous([65536])),
+                          StridedView(w64k, Layout.c_contiguous([65536])))
+    diag = StridedView(m256, Layout.try_new([256], [257], 0))
+    maps = {kind: S.PreparedMap(dev, kind, StridedView(v64k, Layout.c_contiguous([65536])))
+            for kind in (N.MAP_NORM_L1, N.MAP_NORM_L2, N.MAP_NORM_MAX)}
+    p_trace = S.PreparedMap(dev, N.MAP_SUM, diag)
+    cases = {
+        "sum f32 N=2^20 (prepared)": (lambda: fops.dispatch_full(dev, p_sum, stream=sp), out1),
+        "axis-0 sum 256x256 f32 (prepared)": (lambda: aops.dispatch_prepared(dev, p_axis["sum"], stream=sp), None),
+        "axis-0 min 256x256 f32 (prepared)": (lambda: aops.dispatch_prepared(dev, p_axis["min"], stream=sp), None),
+        "axis-0 max 256x256 f32 (prepared)": (lambda: aops.dispatch_prepared(dev, p_axis["max"], stream=sp), None),
+        "axis-0 mean 256x256 f32 (prepared)": (lambda: aops.dispatch_prepared(dev, p_mean, stream=sp), None),
+        "cumsum 256x256 f32 axis 1": (lambda: sops.dispatch_scan(dev, p_scan, stream=sp), None),
+        "dot f32 N=65536": (lambda: p_dot.dispatch(stream=sp), p_dot.output()),
+        "trace 256x256 f32": (lambda: p_trace.dispatch(stream=sp), p_trace.output()),
+        "norm L1 f32 N=65536": (lambda: maps[N.MAP_NORM_L1].dispatch(stream=sp), maps[N.MAP_NORM_L1].output()),
+        "norm L2 f32 N=65536": (lambda: maps[N.MAP_NORM_L2].dispatch(stream=sp), maps[N.MAP_NORM_L2].output()),
+        "norm max f32 N=65536": (lambda: maps[N.MAP_NORM_MAX].dispatch(stream=sp), maps[N.MAP_NORM_MAX].output()),
+    }
+    results = []
+    host = np.empty(1, np.float32)
+    for name, ref_us in PUBLISHED:
+        fn, scalar = cases[name]
+        with torch.cuda.stream(stream):
+            for _ in range(5):
+                fn()
+            dev.synchronize_stream(sp)
+            ds = []
+            for _ in range(30):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda._sleep(50_000)
+                a.record(stream)
+                fn()
+                b.record(stream)
+                b.synchronize()
+                ds.append(a.elapsed_time(b) * 1e3)
+            hs = []
+            for _ in range(30):
+                t0 = time.perf_counter()
+                fn()
+                dev.synchronize_stream(sp)
+                if scalar is not None:
+                    dev.download(scalar, host)  # the value a caller reads back
+                hs.append((time.perf_counter() - t0) * 1e6)
+        results.append({"case": name, "reference_wgpu_rtx5080_us": ref_us,
+                        "device_us": round(statistics.median(ds), 2), "host_us": round(statistics.median(hs), 2)})
+    print(json.dumps({"mode": "published_cases", "gpu": torch.cuda.get_device_name(0), "cases": results}),
+          flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.published:
+        return run_published(args)
     cfg = dict(CONFIGS[args.config])
     if args.misalign:
         if args.config not in (3, 4):

@@ -264,6 +264,111 @@ __global__ void __launch_bounds__(kColThreads)
     }
 }
 
+// Small column reductions in ONE launch: a CTA covers 32 column vectors (V
+// columns each when VEC), its 8 warps stride over the rows (warp w takes rows
+// w, w+8, ...), and the per-warp partials are folded in shared memory in warp
+// order (index-aware for arg-reductions, so the lowest row index wins ties).
+// No row split, no second kernel: for a 256 x 256 matrix the whole reduction
+// is two CTAs and one launch.
+constexpr int kTileWarps = 8;
+template <typename T, int OP, bool ARG, bool VEC, bool MEAN>
+__global__ void __launch_bounds__(32 * kTileWarps)
+    col_tile_kernel(const T *__restrict__ in, AxisArgs a, T *__restrict__ out, uint32_t *__restrict__ idx) {
+    constexpr int V = VEC ? Vec16<T>::V : 1;
+    constexpr int U = 4;
+    __shared__ T s_acc[kTileWarps][32 * V];
+    __shared__ uint32_t s_idx[ARG ? kTileWarps : 1][ARG ? 32 * V : 1];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t lead = VEC ? a.lead : 0;
+    const uint64_t o0 = ((uint64_t)blockIdx.x * 32 + lane) * V;  // virtual column of element 0 of this lane
+    uint32_t vmask = 0;
+#pragma unroll
+    for (int c = 0; c < V; ++c)
+        if (o0 + c >= lead && o0 + c < lead + a.outer) vmask |= 1u << c;
+    T acc[V];
+    uint32_t best[V];
+#pragma unroll
+    for (int c = 0; c < V; ++c) {
+        acc[c] = ARG ? T(0) : identity<T, OP>();
+        best[c] = 0xffffffffu;
+    }
+    auto take = [&](int c, T v, uint64_t r) {
+        if constexpr (ARG) {
+            if (best[c] == 0xffffffffu || (OP == OP_MAX ? v > acc[c] : v < acc[c])) {
+                acc[c] = v;
+                best[c] = (uint32_t)r;
+            }
+        } else {
+            acc[c] = combine<T, OP>(acc[c], v);
+        }
+    };
+    if (vmask) {
+        if constexpr (VEC) {
+            const T *col = in + a.in_base - (int64_t)lead + (int64_t)o0;
+            uint64_t r = warp;
+            for (; r + (U - 1) * kTileWarps < a.len; r += U * kTileWarps) {
+                uint4 raw[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u)
+                    raw[u] = ld_stream(reinterpret_cast<const uint4 *>(col + (int64_t)(r + u * kTileWarps) * a.in_r));
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    Vec16<T> e = as_elems<T>(raw[u]);
+#pragma unroll
+                    for (int c = 0; c < V; ++c)
+                        if ((vmask >> c) & 1u) take(c, e.e[c], r + u * kTileWarps);
+                }
+            }
+            for (; r < a.len; r += kTileWarps) {
+                Vec16<T> e = as_elems<T>(ld_stream(reinterpret_cast<const uint4 *>(col + (int64_t)r * a.in_r)));
+#pragma unroll
+                for (int c = 0; c < V; ++c)
+                    if ((vmask >> c) & 1u) take(c, e.e[c], r);
+            }
+        } else {
+            const T *col = in + a.in_base + (int64_t)o0 * a.in_o;
+            uint64_t r = warp;
+            for (; r + (U - 1) * kTileWarps < a.len; r += U * kTileWarps) {
+                T x[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) x[u] = __ldg(col + (int64_t)(r + u * kTileWarps) * a.in_r);
+#pragma unroll
+                for (int u = 0; u < U; ++u) take(0, x[u], r + u * kTileWarps);
+            }
+            for (; r < a.len; r += kTileWarps) take(0, __ldg(col + (int64_t)r * a.in_r), r);
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < V; ++c) {
+        s_acc[warp][lane * V + c] = acc[c];
+        if constexpr (ARG) s_idx[warp][lane * V + c] = best[c];
+    }
+    __syncthreads();
+    // Thread t folds column t of the CTA over the warps, in warp order.
+    for (int t = threadIdx.x; t < 32 * V; t += 32 * kTileWarps) {
+        const uint64_t vcol = (uint64_t)blockIdx.x * 32 * V + t;
+        if (vcol < lead || vcol >= lead + a.outer) continue;
+        const uint64_t o = vcol - lead;
+        T f = ARG ? T(0) : identity<T, OP>();
+        uint32_t fi = 0xffffffffu;
+        for (int w = 0; w < kTileWarps; ++w) {
+            const T v = s_acc[w][t];
+            if constexpr (ARG) {
+                const uint32_t i = s_idx[w][t];
+                if (i != 0xffffffffu && (fi == 0xffffffffu || arg_better<T, OP>(v, i, f, fi))) {
+                    f = v;
+                    fi = i;
+                }
+            } else {
+                f = combine<T, OP>(f, v);
+            }
+        }
+        if (ARG && fi == 0xffffffffu) f = (OP == OP_MAX) ? Limits<T>::lowest() : Limits<T>::highest();
+        out[a.out_base + (int64_t)o * a.out_o] = finish_value<T, OP, MEAN>(f, a.len);
+        if constexpr (ARG) idx[a.idx_base + (int64_t)o * a.idx_o] = fi;
+    }
+}
+
 // ------------------------------------------------------------------ launch
 
 
@@ -337,6 +442,18 @@ static heph_status launch_axis_typed(Device *dev, cudaStream_t stream, const T *
                         (p.len <= 1 || ((uint64_t)p.in_r * sizeof(T)) % 16 == 0);
     const uint64_t lead = vec_ok ? (reinterpret_cast<uintptr_t>(in + p.in_base) & 15u) / sizeof(T) : 0;
     a.lead = lead;
+    if (p.outer == 0) return HEPH_OK;
+    if (p.len <= 1024 && p.len * p.outer <= (1u << 20)) {
+        // Small: one launch of column tiles, rows spread over the CTA's warps.
+        const uint64_t per_cta = 32 * (vec_ok ? (uint64_t)V : 1);
+        const uint64_t ctas = (lead + p.outer + per_cta - 1) / per_cta;
+        if (vec_ok)
+            col_tile_kernel<T, OP, ARG, true, MEAN><<<(unsigned)ctas, 32 * kTileWarps, 0, stream>>>(in, a, out, idx);
+        else
+            col_tile_kernel<T, OP, ARG, false, MEAN><<<(unsigned)ctas, 32 * kTileWarps, 0, stream>>>(in, a, out, idx);
+        HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "column reduction launch");
+        return HEPH_OK;
+    }
     std::lock_guard<std::mutex> lock(dev->mu);
     // One launch: vectors over all outputs (edge vectors masked), or scalar.
     struct Part {
