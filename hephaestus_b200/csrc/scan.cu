@@ -143,6 +143,22 @@ template <typename T, int JV> struct TileScan {
     T wpre, agg;
 };
 
+// The in-vector inclusive scans of a tile (in place), in logical order.
+template <typename T, int OP, int JV, bool REV>
+__device__ __forceinline__ void vector_local_scan(T (&x)[JV][ScanShape<T, JV>::V]) {
+    constexpr int V = ScanShape<T, JV>::V;
+#pragma unroll
+    for (int j = 0; j < JV; ++j) {
+        if (!REV) {
+#pragma unroll
+            for (int c = 1; c < V; ++c) x[j][c] = combine<T, OP>(x[j][c - 1], x[j][c]);
+        } else {
+#pragma unroll
+            for (int c = V - 2; c >= 0; --c) x[j][c] = combine<T, OP>(x[j][c + 1], x[j][c]);
+        }
+    }
+}
+
 template <typename T, int OP, int JV, bool REV>
 __device__ __forceinline__ void tile_local_scan(T (&x)[JV][ScanShape<T, JV>::V], T *s_warp, TileScan<T, JV> &r) {
     constexpr bool rev = REV;
@@ -465,44 +481,47 @@ __device__ __forceinline__ void chunk_stage_in(const ChunkParams<T> &p, int b, u
     if (hi - lo == p.part) bulk_load(buf + k * p.part, p.in + lo, (uint32_t)(p.part * sizeof(T)), &bar[k]);
 }
 
-// Step 1 of a chunk: total of CTA b's part of logical chunk c, published.
-template <typename T, int OP>
-__device__ __forceinline__ void chunk_reduce_part(const ChunkParams<T> &p, int b, uint64_t c, const T *buf,
-                                                  uint64_t *bar, uint32_t &phases, T *s_red) {
-    constexpr int V = Vec16<T>::V;
+// A staged part is exactly kTilesPerPart tiles.
+constexpr int kTilesPerPart = 2;
+
+// Step 1 of a chunk for CTA b's part of logical chunk c: everything of the
+// part's tile scans that does not depend on the incoming prefix - in-vector
+// scans, warp scans of the vector totals, fold of the warp totals - kept in
+// `rs` for step 3 one iteration later, and the part total (the fold of the
+// tile aggregates) published.  A ragged part (the line's last, read from
+// global memory) only publishes its total; step 3 scans it from scratch.
+template <typename T, int OP, int JV, bool REV>
+__device__ __forceinline__ void chunk_prescan_part(const ChunkParams<T> &p, int b, uint64_t c, const T *buf,
+                                                   uint64_t *bar, uint32_t &phases, T (*s_warp)[kScanWarps],
+                                                   int &parity, T *s_red, TileScan<T, JV> (&rs)[kTilesPerPart]) {
+    constexpr int TILE = ScanShape<T, JV>::TILE;
     uint64_t lo, hi;
     chunk_part_range(p, b, c, lo, hi);
     const uint64_t n = hi - lo;
-    T acc = identity<T, OP>();
     if (n == p.part) {
         const int k = (int)(c % p.buffers);
         mbar_wait(&bar[k], (phases >> k) & 1u, p.err);
         phases ^= 1u << k;
-        // Explicit shared-space loads, 32-bit offsets; the part is a whole
-        // number of 16 KiB tiles, so 1024 vectors per step divide it.
-        const uint32_t a0 = (uint32_t)__cvta_generic_to_shared(buf + k * p.part) + threadIdx.x * 16u;
-        const uint32_t nbytes = (uint32_t)(n * sizeof(T));
-#pragma unroll 2
-        for (uint32_t off = 0; off < nbytes; off += kScanThreads * 16u * 4u) {
-            uint4 r[4];
+        const int base = tile_base_pos<T, JV>(threadIdx.x >> 5, threadIdx.x & 31);
+        T agg = identity<T, OP>();
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-                asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                             : "=r"(r[u].x), "=r"(r[u].y), "=r"(r[u].z), "=r"(r[u].w)
-                             : "r"(a0 + off + u * kScanThreads * 16u));
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                Vec16<T> e = as_elems<T>(r[u]);
-#pragma unroll
-                for (int t = 0; t < V; ++t) acc = combine<T, OP>(acc, e.e[t]);
-            }
+        for (int tl = 0; tl < kTilesPerPart; ++tl) {
+            const int tp = REV ? kTilesPerPart - 1 - tl : tl;
+            T x[JV][ScanShape<T, JV>::V];
+            load_tile_smem<T, JV>(buf + k * p.part + tp * TILE, base, x);
+            tile_local_scan<T, OP, JV, REV>(x, s_warp[parity], rs[tp]);
+            parity ^= 1;
+            agg = combine<T, OP>(agg, rs[tp].agg);
         }
-    } else {
-        for (uint64_t e = lo + threadIdx.x; e < hi; e += kScanThreads) acc = combine<T, OP>(acc, p.in[e]);
+        if (threadIdx.x == 0) publish(p.status, c * gridDim.x + b, kStatePrefix, agg);
+        return;
     }
-    // Only thread 0 needs the CTA total: one barrier, no trailing one (the
-    // caller alternates s_red by chunk parity, and the reduces of chunks c and
-    // c + 2 are separated by barriers).
+    constexpr int V = Vec16<T>::V;
+    (void)V;
+    T acc = identity<T, OP>();
+    for (uint64_t e = lo + threadIdx.x; e < hi; e += kScanThreads) acc = combine<T, OP>(acc, p.in[e]);
+    // One barrier, no trailing one: s_red is rewritten only by the next
+    // ragged part, which cannot come before the next barriers.
     acc = warp_fold<T, OP>(acc);
     if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = acc;
     __syncthreads();
@@ -522,7 +541,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
     T *buf = reinterpret_cast<T *>(dyn_smem);  // buffers x part elements
     __shared__ uint64_t bar[kChunkMaxBuffers];
     __shared__ T s_warp[2][kScanWarps];
-    __shared__ T s_red[2][kScanWarps];  // by chunk parity: consecutive part reduces have no barrier between
+    __shared__ T s_red[kScanWarps];
     __shared__ T s_pair[2][kScanWarps];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int G = gridDim.x, b = blockIdx.x;
@@ -530,6 +549,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
     constexpr bool rev = REV;
     const int base = tile_base_pos<T, JV>(warp, lane);
     uint32_t phases = 0;
+    int parity = 0;
 
     if (threadIdx.x == 0) {
         for (int k = 0; k < NB; ++k) mbar_init(&bar[k], 1);
@@ -539,12 +559,14 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
     __syncthreads();
 
     T carry = p.carry ? *p.carry : identity<T, OP>();
-    if (p.nchunks > 0) chunk_reduce_part<T, OP>(p, b, 0, buf, bar, phases, s_red[0]);
-    int parity = 0;
+    // Prefix-independent tile-scan results of the part scanned in this
+    // iteration (cur) and of the next one (nxt).
+    TileScan<T, JV> cur[kTilesPerPart], nxt[kTilesPerPart];
+    if (p.nchunks > 0) chunk_prescan_part<T, OP, JV, REV>(p, b, 0, buf, bar, phases, s_warp, parity, s_red, cur);
     for (uint64_t c = 0; c < p.nchunks; ++c) {
         // The part totals of chunk c were published one iteration ago: for
-        // 4-byte T their status words are loaded here, before the part
-        // reduce, so the L2 round trip overlaps it.
+        // 4-byte T their status words are loaded here, before step 1, so the
+        // L2 round trip overlaps it.
         unsigned long long early[kChunkMaxPartsPerThread];
         if constexpr (sizeof(T) == 4) {
 #pragma unroll
@@ -558,7 +580,9 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
                                  : "memory");
             }
         }
-        if (c + 1 < p.nchunks) chunk_reduce_part<T, OP>(p, b, c + 1, buf, bar, phases, s_red[(c + 1) & 1]);
+        // Step 1: prescan of the next part, its total published.
+        if (c + 1 < p.nchunks)
+            chunk_prescan_part<T, OP, JV, REV>(p, b, c + 1, buf, bar, phases, s_warp, parity, s_red, nxt);
 
         // Step 2: the part totals of chunk c.
         T before = identity<T, OP>(), total = identity<T, OP>();
@@ -589,7 +613,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
             if (rev ? (q > b) : (q < b)) before = combine<T, OP>(before, v);
         }
         // Both folds share one barrier; s_pair is rewritten only in the next
-        // iteration, after the tile scans' barriers.
+        // iteration, after step 1's barriers.
         before = warp_fold<T, OP>(before);
         total = warp_fold<T, OP>(total);
         if (lane == 0) {
@@ -607,38 +631,56 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
         T run = combine<T, OP>(carry, before);
         carry = combine<T, OP>(carry, total);
 
-        // Step 3: scan the part in tiles, in logical order.
+        // Step 3: the part's outputs, tile by tile in logical order.
         uint64_t lo, hi;
         chunk_part_range(p, b, c, lo, hi);
-        const bool staged = hi - lo == p.part;  // landed: step 1 waited for it
-        const T *src = staged ? buf + (c % NB) * p.part : p.in + lo;
-        const uint64_t ntiles = (hi - lo + TILE - 1) / TILE;
-        for (uint64_t tl = 0; tl < ntiles; ++tl) {
-            const uint64_t tp = rev ? ntiles - 1 - tl : tl;
-            const uint64_t start = tp * TILE;  // relative to lo
-            const uint64_t valid = min((uint64_t)TILE, hi - lo - start);
-            const bool full = valid == (uint64_t)TILE;
-            T x[JV][V];
-            if (staged) load_tile_smem<T, JV>(src + start, base, x);
-            else if (full) load_tile_vec<T, JV>(src + start, base, x, false);
-            else load_tile_scalar<T, OP, JV>(src + start, valid, base, x);
-            TileScan<T, JV> r;
-            tile_local_scan<T, OP, JV, REV>(x, s_warp[parity], r);
-            parity ^= 1;
-            // Past the last tile's barrier every thread has read the part out
-            // of buffer c%NB: refill it with chunk c+NB now, so the copy is in
-            // flight while the last tile is finished and stored.
-            if (tl + 1 == ntiles && threadIdx.x == 0 && c + NB < p.nchunks) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                chunk_stage_in(p, b, c + NB, buf, bar);
+        if (hi - lo == p.part) {
+            // Staged and prescanned: reload, redo the in-vector scans, add
+            // the prefixes.  No barrier.
+            const T *src = buf + (c % NB) * p.part;
+#pragma unroll
+            for (int tl = 0; tl < kTilesPerPart; ++tl) {
+                const int tp = rev ? kTilesPerPart - 1 - tl : tl;
+                T x[JV][V];
+                load_tile_smem<T, JV>(src + tp * TILE, base, x);
+                if (tl + 1 == kTilesPerPart) {
+                    // Every thread has read the part: refill its buffer with
+                    // chunk c+NB while the outputs are finished and stored.
+                    __syncthreads();
+                    if (threadIdx.x == 0 && c + NB < p.nchunks) {
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        chunk_stage_in(p, b, c + NB, buf, bar);
+                    }
+                }
+                vector_local_scan<T, OP, JV, REV>(x);
+                T y[JV][V];
+                tile_outputs<T, OP, JV, REV, EXCL>(x, cur[tp], run, y);
+                run = combine<T, OP>(run, cur[tp].agg);
+                store_tile<T, JV>(p.out + lo + (uint64_t)tp * TILE, TILE, true, base, y, p.store_mode);
             }
-            T y[JV][V];
-            tile_outputs<T, OP, JV, REV, EXCL>(x, r, run, y);
-            run = combine<T, OP>(run, r.agg);
-            store_tile<T, JV>(p.out + lo + start, valid, full, base, y, p.store_mode);
+        } else {
+            const uint64_t ntiles = (hi - lo + TILE - 1) / TILE;
+            for (uint64_t tl = 0; tl < ntiles; ++tl) {
+                const uint64_t tp = rev ? ntiles - 1 - tl : tl;
+                const uint64_t start = tp * TILE;  // relative to lo
+                const uint64_t valid = min((uint64_t)TILE, hi - lo - start);
+                const bool full = valid == (uint64_t)TILE;
+                T x[JV][V];
+                if (full) load_tile_vec<T, JV>(p.in + lo + start, base, x, false);
+                else load_tile_scalar<T, OP, JV>(p.in + lo + start, valid, base, x);
+                TileScan<T, JV> r;
+                tile_local_scan<T, OP, JV, REV>(x, s_warp[parity], r);
+                parity ^= 1;
+                T y[JV][V];
+                tile_outputs<T, OP, JV, REV, EXCL>(x, r, run, y);
+                run = combine<T, OP>(run, r.agg);
+                store_tile<T, JV>(p.out + lo + start, valid, full, base, y, p.store_mode);
+            }
+            // A ragged or empty part never used its buffer.
+            if (threadIdx.x == 0 && c + NB < p.nchunks) chunk_stage_in(p, b, c + NB, buf, bar);
         }
-        // An empty part (past the end of the line) never used its buffer.
-        if (ntiles == 0 && threadIdx.x == 0 && c + NB < p.nchunks) chunk_stage_in(p, b, c + NB, buf, bar);
+#pragma unroll
+        for (int t = 0; t < kTilesPerPart; ++t) cur[t] = nxt[t];
     }
 }
 
@@ -707,9 +749,8 @@ template <typename T, int OP, bool REV, bool EXCL>
 static bool launch_chunked(Device *dev, cudaStream_t stream, const T *in, T *out, uint64_t len, bool reverse,
                            bool exclusive, const T *carry, heph_status *st) {
     using S = ScanShape<T, kChunkVectors>;
-    const int nb = std::min(kChunkMaxBuffers, std::max(2, scan_knob("HEPH_SCAN_BUFS", 3)));
-    const uint64_t part_bytes = (uint64_t)std::max(16, scan_knob("HEPH_SCAN_PART_KB", 32)) << 10;
-    const uint64_t part = std::max<uint64_t>(1, part_bytes / sizeof(T) / S::TILE) * S::TILE;
+    const int nb = std::min(kChunkMaxBuffers, std::max(3, scan_knob("HEPH_SCAN_BUFS", 3)));
+    const uint64_t part = (uint64_t)kTilesPerPart * S::TILE;  // 32 KiB
     const size_t smem = (size_t)nb * part * sizeof(T);
     if (smem > (200u << 10)) return false;
     auto kernel = scan_chunked_kernel<T, OP, kChunkVectors, REV, EXCL>;
