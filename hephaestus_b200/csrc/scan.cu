@@ -279,7 +279,7 @@ __device__ __forceinline__ void load_tile_scalar(const T *src, uint64_t valid, i
 
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t pol;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));  // pure: hoisted and shared
     return pol;
 }
 __device__ __forceinline__ void st_policy(uint4 *p, uint4 v, uint64_t pol) {
