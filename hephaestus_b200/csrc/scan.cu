@@ -481,8 +481,6 @@ __device__ __forceinline__ void chunk_stage_in(const ChunkParams<T> &p, int b, u
     if (hi - lo == p.part) bulk_load(buf + k * p.part, p.in + lo, (uint32_t)(p.part * sizeof(T)), &bar[k]);
 }
 
-// A staged part is exactly kTilesPerPart tiles.
-constexpr int kTilesPerPart = 2;
 
 // Step 1 of a chunk for CTA b's part of logical chunk c: everything of the
 // part's tile scans that does not depend on the incoming prefix - in-vector
@@ -490,10 +488,10 @@ constexpr int kTilesPerPart = 2;
 // `rs` for step 3 one iteration later, and the part total (the fold of the
 // tile aggregates) published.  A ragged part (the line's last, read from
 // global memory) only publishes its total; step 3 scans it from scratch.
-template <typename T, int OP, int JV, bool REV>
+template <typename T, int OP, int JV, bool REV, int TPP>
 __device__ __forceinline__ void chunk_prescan_part(const ChunkParams<T> &p, int b, uint64_t c, const T *buf,
                                                    uint64_t *bar, uint32_t &phases, T (*s_warp)[kScanWarps],
-                                                   int &parity, T *s_red, TileScan<T, JV> (&rs)[kTilesPerPart]) {
+                                                   int &parity, T *s_red, TileScan<T, JV> (&rs)[TPP]) {
     constexpr int TILE = ScanShape<T, JV>::TILE;
     uint64_t lo, hi;
     chunk_part_range(p, b, c, lo, hi);
@@ -505,8 +503,8 @@ __device__ __forceinline__ void chunk_prescan_part(const ChunkParams<T> &p, int 
         const int base = tile_base_pos<T, JV>(threadIdx.x >> 5, threadIdx.x & 31);
         T agg = identity<T, OP>();
 #pragma unroll
-        for (int tl = 0; tl < kTilesPerPart; ++tl) {
-            const int tp = REV ? kTilesPerPart - 1 - tl : tl;
+        for (int tl = 0; tl < TPP; ++tl) {
+            const int tp = REV ? TPP - 1 - tl : tl;
             T x[JV][ScanShape<T, JV>::V];
             load_tile_smem<T, JV>(buf + k * p.part + tp * TILE, base, x);
             tile_local_scan<T, OP, JV, REV>(x, s_warp[parity], rs[tp]);
@@ -533,8 +531,11 @@ __device__ __forceinline__ void chunk_prescan_part(const ChunkParams<T> &p, int 
     }
 }
 
-template <typename T, int OP, int JV, bool REV, bool EXCL>
-__global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkParams<T> p) {
+// L: parts prescanned ahead (their totals are published L iterations before
+// the exchange that reads them - the slack a late CTA can use); TPP: tiles
+// per staged part.  Needs p.buffers >= L + 2.
+template <typename T, int OP, int JV, bool REV, bool EXCL, int L, int TPP>
+__global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const ChunkParams<T> p) {
     using S = ScanShape<T, JV>;
     constexpr int V = S::V, TILE = S::TILE;
     extern __shared__ __align__(128) unsigned char dyn_smem[];
@@ -559,10 +560,14 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
     __syncthreads();
 
     T carry = p.carry ? *p.carry : identity<T, OP>();
-    // Prefix-independent tile-scan results of the part scanned in this
-    // iteration (cur) and of the next one (nxt).
-    TileScan<T, JV> cur[kTilesPerPart], nxt[kTilesPerPart];
-    if (p.nchunks > 0) chunk_prescan_part<T, OP, JV, REV>(p, b, 0, buf, bar, phases, s_warp, parity, s_red, cur);
+    // Prefix-independent tile-scan results of the parts of chunks c .. c+L:
+    // ring[0] is output in this iteration, ring[L] is prescanned in it.  The
+    // ring shifts with constant indices (registers, no local memory).
+    TileScan<T, JV> ring[L + 1][TPP];
+#pragma unroll
+    for (int k = 0; k < L; ++k)
+        if ((uint64_t)k < p.nchunks)
+            chunk_prescan_part<T, OP, JV, REV, TPP>(p, b, k, buf, bar, phases, s_warp, parity, s_red, ring[k]);
     for (uint64_t c = 0; c < p.nchunks; ++c) {
         // The part totals of chunk c were published one iteration ago: for
         // 4-byte T their status words are loaded here, before step 1, so the
@@ -580,9 +585,9 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
                                  : "memory");
             }
         }
-        // Step 1: prescan of the next part, its total published.
-        if (c + 1 < p.nchunks)
-            chunk_prescan_part<T, OP, JV, REV>(p, b, c + 1, buf, bar, phases, s_warp, parity, s_red, nxt);
+        // Step 1: prescan of the part L chunks ahead, its total published.
+        if (c + L < p.nchunks)
+            chunk_prescan_part<T, OP, JV, REV, TPP>(p, b, c + L, buf, bar, phases, s_warp, parity, s_red, ring[L]);
 
         // Step 2: the part totals of chunk c.
         T before = identity<T, OP>(), total = identity<T, OP>();
@@ -639,11 +644,11 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
             // the prefixes.  No barrier.
             const T *src = buf + (c % NB) * p.part;
 #pragma unroll
-            for (int tl = 0; tl < kTilesPerPart; ++tl) {
-                const int tp = rev ? kTilesPerPart - 1 - tl : tl;
+            for (int tl = 0; tl < TPP; ++tl) {
+                const int tp = rev ? TPP - 1 - tl : tl;
                 T x[JV][V];
                 load_tile_smem<T, JV>(src + tp * TILE, base, x);
-                if (tl + 1 == kTilesPerPart) {
+                if (tl + 1 == TPP) {
                     // Every thread has read the part: refill its buffer with
                     // chunk c+NB while the outputs are finished and stored.
                     __syncthreads();
@@ -654,8 +659,8 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
                 }
                 vector_local_scan<T, OP, JV, REV>(x);
                 T y[JV][V];
-                tile_outputs<T, OP, JV, REV, EXCL>(x, cur[tp], run, y);
-                run = combine<T, OP>(run, cur[tp].agg);
+                tile_outputs<T, OP, JV, REV, EXCL>(x, ring[0][tp], run, y);
+                run = combine<T, OP>(run, ring[0][tp].agg);
                 store_tile<T, JV>(p.out + lo + (uint64_t)tp * TILE, TILE, true, base, y, p.store_mode);
             }
         } else {
@@ -680,7 +685,9 @@ __global__ void __launch_bounds__(kScanThreads) scan_chunked_kernel(const ChunkP
             if (threadIdx.x == 0 && c + NB < p.nchunks) chunk_stage_in(p, b, c + NB, buf, bar);
         }
 #pragma unroll
-        for (int t = 0; t < kTilesPerPart; ++t) cur[t] = nxt[t];
+        for (int k = 0; k < L; ++k)
+#pragma unroll
+            for (int t = 0; t < TPP; ++t) ring[k][t] = ring[k + 1][t];
     }
 }
 
@@ -745,15 +752,15 @@ static heph_status status_for(Device *dev, cudaStream_t stream, uint64_t entries
 
 // The chunked kernel for one long aligned line.  Returns false (nothing
 // launched) when the line is too short to give every CTA four parts.
-template <typename T, int OP, bool REV, bool EXCL>
+template <typename T, int OP, bool REV, bool EXCL, int L, int TPP>
 static bool launch_chunked(Device *dev, cudaStream_t stream, const T *in, T *out, uint64_t len, bool reverse,
-                           bool exclusive, const T *carry, heph_status *st) {
+                           bool exclusive, const T *carry, heph_status *st, int default_ctas) {
     using S = ScanShape<T, kChunkVectors>;
-    const int nb = std::min(kChunkMaxBuffers, std::max(3, scan_knob("HEPH_SCAN_BUFS", 3)));
-    const uint64_t part = (uint64_t)kTilesPerPart * S::TILE;  // 32 KiB
+    const int nb = std::min(kChunkMaxBuffers, std::max(L + 2, scan_knob("HEPH_SCAN_BUFS", L + 2)));
+    const uint64_t part = (uint64_t)TPP * S::TILE;
     const size_t smem = (size_t)nb * part * sizeof(T);
     if (smem > (200u << 10)) return false;
-    auto kernel = scan_chunked_kernel<T, OP, kChunkVectors, REV, EXCL>;
+    auto kernel = scan_chunked_kernel<T, OP, kChunkVectors, REV, EXCL, L, TPP>;
     int nb_sm = 0;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb_sm, kernel, kScanThreads, smem) != cudaSuccess ||
@@ -761,7 +768,7 @@ static bool launch_chunked(Device *dev, cudaStream_t stream, const T *in, T *out
         cudaGetLastError();
         return false;
     }
-    const int per_sm = std::min(nb_sm, std::max(1, scan_knob("HEPH_SCAN_CHUNK_CTAS", 2)));
+    const int per_sm = std::min(nb_sm, std::max(1, scan_knob("HEPH_SCAN_CHUNK_CTAS", default_ctas)));
     const uint64_t G =
         std::min<uint64_t>((uint64_t)dev->sm_count * per_sm, (uint64_t)kChunkMaxPartsPerThread * kScanThreads);
     if (len < 4 * part * G) return false;
@@ -789,6 +796,22 @@ static bool launch_chunked(Device *dev, cudaStream_t stream, const T *in, T *out
     return true;
 }
 
+// Shape of the chunked scan: parts are one 16 KiB tile, prescanned two
+// chunks ahead, four part buffers (64 KiB) per CTA, three CTAs per SM.  Of
+// the shapes measured - lookahead 1-3, 1-2 tiles per part, 1-4 CTAs per SM -
+// this one streams fastest: the two-chunk slack absorbs late CTAs at the
+// part-total exchange, and 24 warps per SM hide the tile-scan latency.
+constexpr int kChunkLookahead = 2;
+constexpr int kChunkTilesPerPart = 1;
+constexpr int kChunkCtasPerSm = 3;
+
+template <typename T, int OP, bool REV, bool EXCL>
+static bool launch_chunked_any(Device *dev, cudaStream_t stream, const T *in, T *out, uint64_t len, bool reverse,
+                               bool exclusive, const T *carry, heph_status *st) {
+    return launch_chunked<T, OP, REV, EXCL, kChunkLookahead, kChunkTilesPerPart>(dev, stream, in, out, len, reverse,
+                                                                                exclusive, carry, st, kChunkCtasPerSm);
+}
+
 template <typename T, int OP>
 static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *in, T *out, const AxisProblem &pr,
                                      bool reverse, bool exclusive, const T *carry) {
@@ -813,11 +836,11 @@ static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *
         const T *ci = in + pr.in_base;
         T *co = out + pr.out_base;
         if (reverse)
-            launched = exclusive ? launch_chunked<T, OP, true, true>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st)
-                                 : launch_chunked<T, OP, true, false>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st);
+            launched = exclusive ? launch_chunked_any<T, OP, true, true>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st)
+                                 : launch_chunked_any<T, OP, true, false>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st);
         else
-            launched = exclusive ? launch_chunked<T, OP, false, true>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st)
-                                 : launch_chunked<T, OP, false, false>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st);
+            launched = exclusive ? launch_chunked_any<T, OP, false, true>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st)
+                                 : launch_chunked_any<T, OP, false, false>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st);
         if (launched) return st;
     }
     const uint64_t tiles_per_line = (pr.len + S::TILE - 1) / S::TILE;
