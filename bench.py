@@ -173,8 +173,11 @@ class ClockSampler:
 
 def cpu_sample(cfg_id: int, cfg: dict, oracle, seconds: float = 10.0, threads: int = 0):
     """Time the oracle's multithreaded restatement on a bounded sample.
-    Returns (GB/s, cores, sample description)."""
-    cores = oracle.max_threads() if threads == 0 else threads
+    Returns (GB/s, cores, sample description).  threads=0 means every host
+    core this process may run on: the count is passed to the oracle
+    explicitly, so torchrun's OMP_NUM_THREADS=1 does not shrink the sample."""
+    threads = threads or len(os.sched_getaffinity(0))
+    cores = threads
     if cfg_id == 2 or cfg_id == 5:
         n = 1 << 26
         dt = np.uint32 if cfg_id == 2 else np.int32

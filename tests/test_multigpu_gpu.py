@@ -18,7 +18,7 @@ def test_partitioned_scan_and_reduce(tmp_path, oracle):
     world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs two or more GPUs")
-    world = min(world, 4)
+    world = min(world, 8)
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
            "--master-addr", "127.0.0.1", "--master-port", "29533",
