@@ -120,26 +120,29 @@ __global__ void __launch_bounds__(kReduceThreads)
 
 // A fused batch of dense full reductions in one launch: problem p owns CTAs
 // [cta_begin, cta_begin + ctas) of the grid, its own partial slots (indexed
-// like its CTAs) and ticket; a CTA finds its problem by binary search over
-// the table's cta_begin.
+// like its CTAs) and ticket.  A CTA finds its problem with one parallel read
+// of the table (each thread checks one entry), so its first data load waits
+// for a single table load instead of a chain of dependent ones.
 template <typename Tin, typename Tacc, int OP>
 __global__ void __launch_bounds__(kReduceThreads)
     reduce_fused_kernel(const FusedFull *__restrict__ table, uint32_t nprob, Tacc *__restrict__ partials,
                         unsigned int *__restrict__ tickets) {
     __shared__ Tacc scratch[kReduceThreads / 32];
+    __shared__ FusedFull s_f;
     __shared__ uint32_t s_prob;
-    if (threadIdx.x == 0) {
-        uint32_t lo = 0, hi = nprob - 1;
-        while (lo < hi) {
-            const uint32_t mid = (lo + hi + 1) / 2;
-            if (table[mid].cta_begin <= blockIdx.x) lo = mid;
-            else hi = mid - 1;
+    for (uint32_t q0 = 0; q0 < nprob; q0 += kReduceThreads) {
+        const uint32_t q = q0 + threadIdx.x;
+        if (q < nprob) {
+            const FusedFull e = table[q];
+            if (e.cta_begin <= blockIdx.x && blockIdx.x - e.cta_begin < e.ctas) {
+                s_f = e;
+                s_prob = q;
+            }
         }
-        s_prob = lo;
     }
     __syncthreads();
     const uint32_t p = s_prob;
-    const FusedFull f = table[p];
+    const FusedFull f = s_f;
     const unsigned int block = blockIdx.x - f.cta_begin;
     const Tacc acc = dense_fold<Tin, Tacc, OP>(static_cast<const Tin *>(f.in), f.n, block, f.ctas);
     finish_slice<Tacc, OP>(acc, static_cast<Tacc *>(f.out), partials + f.cta_begin, tickets + p, block, f.ctas,
