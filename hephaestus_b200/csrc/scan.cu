@@ -40,7 +40,11 @@ constexpr int kScanThreads = 256;
 constexpr int kScanWarps = kScanThreads / 32;
 constexpr uint32_t kPolls = 1u << 20;        // bounded waits on other CTAs
 constexpr int kLookbackVectors = 8;          // look-back tile: 8 x 128-bit per thread (32 KiB)
-constexpr int kChunkVectors = 4;             // chunked kernel tile: 4 x 128-bit per thread (16 KiB)
+constexpr int kLookbackVectorsSmall = 4;     // look-back tile for lines under 32 KiB (16 KiB)
+constexpr uint64_t kInterleaveMinTiles = 8;  // look-back tiles per line from which lines interleave
+constexpr int kChunkVectors = 4;
+constexpr uint64_t kPerLineChunkedBytes = 128ull << 20;  // see launch_scan_typed
+constexpr int kMaxCachedDevices = 64;        // device ordinals with cached launch queries             // chunked kernel tile: 4 x 128-bit per thread (16 KiB)
 constexpr int kChunkMaxBuffers = 6;          // part buffers per CTA of the chunked scan
 constexpr int kChunkMaxPartsPerThread = 2;   // chunked grids have at most 2 x 256 CTAs
 
@@ -277,6 +281,27 @@ __device__ __forceinline__ void load_tile_scalar(const T *src, uint64_t valid, i
         }
 }
 
+// A partial tile whose start is 16-byte aligned: whole vectors inside
+// `valid` with 128-bit loads, the vector that straddles its end element by
+// element, identity padding beyond it.
+template <typename T, int OP, int JV>
+__device__ __forceinline__ void load_tile_partial_vec(const T *src, uint64_t valid, int base,
+                                                      T (&x)[JV][ScanShape<T, JV>::V]) {
+    constexpr int V = ScanShape<T, JV>::V;
+#pragma unroll
+    for (int j = 0; j < JV; ++j) {
+        const uint64_t pos = (uint64_t)(base + j * 32 * V);
+        if (pos + V <= valid) {
+            Vec16<T> e = as_elems<T>(ld_stream(reinterpret_cast<const uint4 *>(src + pos)));
+#pragma unroll
+            for (int c = 0; c < V; ++c) x[j][c] = e.e[c];
+        } else {
+#pragma unroll
+            for (int c = 0; c < V; ++c) x[j][c] = pos + c < valid ? src[pos + c] : identity<T, OP>();
+        }
+    }
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t pol;
     asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));  // pure: hoisted and shared
@@ -316,6 +341,28 @@ __device__ __forceinline__ void store_tile(T *dst, uint64_t valid, bool full, in
     }
 }
 
+// A partial tile whose start is 16-byte aligned: whole vectors inside
+// `valid` with 128-bit streaming stores, the straddling one element-wise.
+template <typename T, int JV>
+__device__ __forceinline__ void store_tile_partial_vec(T *dst, uint64_t valid, int base,
+                                                       const T (&y)[JV][ScanShape<T, JV>::V]) {
+    constexpr int V = ScanShape<T, JV>::V;
+#pragma unroll
+    for (int j = 0; j < JV; ++j) {
+        const uint64_t pos = (uint64_t)(base + j * 32 * V);
+        if (pos + V <= valid) {
+            Vec16<T> e;
+#pragma unroll
+            for (int c = 0; c < V; ++c) e.e[c] = y[j][c];
+            st_stream(reinterpret_cast<uint4 *>(dst + pos), as_uint4(e));
+        } else {
+#pragma unroll
+            for (int c = 0; c < V; ++c)
+                if (pos + c < valid) dst[pos + c] = y[j][c];
+        }
+    }
+}
+
 // --------------------------------------------------- decoupled look-back
 
 template <typename T> struct LookbackParams {
@@ -323,6 +370,12 @@ template <typename T> struct LookbackParams {
     T *out;
     uint64_t len;               // elements per line
     uint64_t tiles_per_line;
+    uint64_t lines;
+    // Tile numbering: line-major (id = line * tiles_per_line + position) or,
+    // when `interleaved`, position-major (id = position * lines + line).
+    // Either way a tile's predecessors in its line have lower ids.
+    uint64_t pos_step;          // id distance between neighbouring positions: 1, or lines
+    int interleaved;
     int64_t in_line, out_line;  // element distance between line starts
     StatusView status;
     const T *carry;             // nullable seed of line 0
@@ -330,27 +383,29 @@ template <typename T> struct LookbackParams {
     int reverse, exclusive;
 };
 
-// Exclusive prefix of `tile` within its line: fold of the predecessors back
-// to the nearest one that has published its inclusive prefix, 32 predecessors
-// per round trip.  Runs on one warp.
+// Exclusive prefix of `tile` (at position `pos` of its line) within its
+// line: fold of the predecessors back to the nearest one that has published
+// its inclusive prefix, 32 predecessors per round trip.  The predecessor at
+// distance j is tile - j * pos_step.  Runs on one warp.
 template <typename T, int OP>
-__device__ T lookback(const LookbackParams<T> &p, uint64_t tile, uint64_t line_first, int lane) {
+__device__ T lookback(const LookbackParams<T> &p, uint64_t tile, uint64_t pos, int lane) {
     T excl = identity<T, OP>();
-    int64_t cur = (int64_t)tile - 1;
+    int64_t back = 1;  // distance of this round's first predecessor
     uint32_t polls = 0;
     while (true) {
-        const int64_t idx = cur - lane;
-        const bool in_range = idx >= (int64_t)line_first;
+        const int64_t d = back + lane;
+        const bool in_range = d <= (int64_t)pos;
         uint32_t state = kStatePrefix;  // positions before the line start act as an identity prefix
         T val = identity<T, OP>();
-        if (in_range) state = read_status(p.status, (uint64_t)idx, val);
+        const uint64_t idx = tile - (uint64_t)d * p.pos_step;
+        if (in_range) state = read_status(p.status, idx, val);
         while (__any_sync(kFullMask, state == kStateInvalid)) {
             if (++polls > kPolls) {
                 if (lane == 0) raise_device_error(p.err, DEVERR_LOOKBACK_TIMEOUT);
                 return excl;
             }
             __nanosleep(32);
-            if (state == kStateInvalid) state = read_status(p.status, (uint64_t)idx, val);
+            if (state == kStateInvalid) state = read_status(p.status, idx, val);
         }
         const unsigned pm = __ballot_sync(kFullMask, state == kStatePrefix);
         const int stop = pm ? __ffs(pm) - 1 : 31;
@@ -358,11 +413,15 @@ __device__ T lookback(const LookbackParams<T> &p, uint64_t tile, uint64_t line_f
         v = warp_fold<T, OP>(v);
         excl = combine<T, OP>(v, excl);
         if (pm) return excl;
-        cur -= 32;
+        back += 32;
     }
 }
 
-// One tile per CTA; tiles of a line are numbered in scan order.
+// One tile per CTA.  Long lines are numbered position-major (the first tile
+// of every line, then the second, ...) so the resident CTAs advance all
+// lines' prefix chains at once instead of waiting along one line's chain;
+// short lines stay line-major, which keeps the CTAs in flight on one
+// contiguous stretch of memory.
 template <typename T, int OP, bool VEC, int JV, bool REV, bool EXCL>
 __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const LookbackParams<T> p) {
     using S = ScanShape<T, JV>;
@@ -372,8 +431,14 @@ __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const Lookb
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr bool rev = REV;
     const uint64_t tile = blockIdx.x;
-    const uint64_t line = tile / p.tiles_per_line;
-    const uint64_t t_in_line = tile - line * p.tiles_per_line;
+    uint64_t line, t_in_line;
+    if (p.interleaved) {
+        t_in_line = tile / p.lines;
+        line = tile - t_in_line * p.lines;
+    } else {
+        line = tile / p.tiles_per_line;
+        t_in_line = tile - line * p.tiles_per_line;
+    }
     const uint64_t ptile = rev ? p.tiles_per_line - 1 - t_in_line : t_in_line;
     const T *lin = p.in + (int64_t)line * p.in_line;
     T *lout = p.out + (int64_t)line * p.out_line;
@@ -384,6 +449,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const Lookb
 
     T x[JV][V];
     if (full) load_tile_vec<T, JV>(lin + start, base, x, true);
+    else if (VEC) load_tile_partial_vec<T, OP, JV>(lin + start, valid, base, x);
     else load_tile_scalar<T, OP, JV>(lin + start, valid, base, x);
     TileScan<T, JV> r;
     tile_local_scan<T, OP, JV, REV>(x, s_warp, r);
@@ -395,7 +461,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const Lookb
             if (lane == 0) publish(p.status, tile, kStatePrefix, combine<T, OP>(tp, r.agg));
         } else {
             if (lane == 0) publish(p.status, tile, kStateAggregate, r.agg);
-            tp = lookback<T, OP>(p, tile, tile - t_in_line, lane);
+            tp = lookback<T, OP>(p, tile, t_in_line, lane);
             if (lane == 0) publish(p.status, tile, kStatePrefix, combine<T, OP>(tp, r.agg));
         }
         if (lane == 0) s_prefix = tp;
@@ -403,7 +469,8 @@ __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const Lookb
     __syncthreads();
     T y[JV][V];
     tile_outputs<T, OP, JV, REV, EXCL>(x, r, s_prefix, y);
-    store_tile<T, JV>(lout + start, valid, full, base, y);
+    if (VEC && !full) store_tile_partial_vec<T, JV>(lout + start, valid, base, y);
+    else store_tile<T, JV>(lout + start, valid, full, base, y);
 }
 
 // --------------------------------- chunked reduce-then-scan, parts in smem
@@ -761,12 +828,27 @@ static bool launch_chunked(Device *dev, cudaStream_t stream, const T *in, T *out
     const size_t smem = (size_t)nb * part * sizeof(T);
     if (smem > (200u << 10)) return false;
     auto kernel = scan_chunked_kernel<T, OP, kChunkVectors, REV, EXCL, L, TPP>;
+    // The attribute and occupancy queries cost host time on every call (the
+    // GPU idles behind them when lines are launched back to back): they run
+    // once per (device, kernel, shared-memory size).  The caller holds the
+    // device's lock, and each device has its own slot.
+    struct Occupancy {
+        size_t smem;
+        int nb_sm;
+    };
+    static Occupancy occ[kMaxCachedDevices];
     int nb_sm = 0;
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb_sm, kernel, kScanThreads, smem) != cudaSuccess ||
-        nb_sm < 1) {
-        cudaGetLastError();
-        return false;
+    Occupancy *oc = dev->ordinal >= 0 && dev->ordinal < kMaxCachedDevices ? &occ[dev->ordinal] : nullptr;
+    if (oc && oc->nb_sm > 0 && oc->smem == smem) {
+        nb_sm = oc->nb_sm;
+    } else {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb_sm, kernel, kScanThreads, smem) != cudaSuccess ||
+            nb_sm < 1) {
+            cudaGetLastError();
+            return false;
+        }
+        if (oc) *oc = Occupancy{smem, nb_sm};
     }
     const int per_sm = std::min(nb_sm, std::max(1, scan_knob("HEPH_SCAN_CHUNK_CTAS", default_ctas)));
     const uint64_t G =
@@ -812,6 +894,20 @@ static bool launch_chunked_any(Device *dev, cudaStream_t stream, const T *in, T 
                                                                                 exclusive, carry, st, kChunkCtasPerSm);
 }
 
+template <typename T, int OP, int JV>
+static void launch_lookback(int sel, dim3 grid, cudaStream_t stream, const LookbackParams<T> &p) {
+    switch (sel) {
+        case 0: scan_lookback_kernel<T, OP, false, JV, false, false><<<grid, kScanThreads, 0, stream>>>(p); break;
+        case 1: scan_lookback_kernel<T, OP, false, JV, false, true><<<grid, kScanThreads, 0, stream>>>(p); break;
+        case 2: scan_lookback_kernel<T, OP, false, JV, true, false><<<grid, kScanThreads, 0, stream>>>(p); break;
+        case 3: scan_lookback_kernel<T, OP, false, JV, true, true><<<grid, kScanThreads, 0, stream>>>(p); break;
+        case 4: scan_lookback_kernel<T, OP, true, JV, false, false><<<grid, kScanThreads, 0, stream>>>(p); break;
+        case 5: scan_lookback_kernel<T, OP, true, JV, false, true><<<grid, kScanThreads, 0, stream>>>(p); break;
+        case 6: scan_lookback_kernel<T, OP, true, JV, true, false><<<grid, kScanThreads, 0, stream>>>(p); break;
+        default: scan_lookback_kernel<T, OP, true, JV, true, true><<<grid, kScanThreads, 0, stream>>>(p); break;
+    }
+}
+
 template <typename T, int OP>
 static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *in, T *out, const AxisProblem &pr,
                                      bool reverse, bool exclusive, const T *carry) {
@@ -830,20 +926,36 @@ static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *
                      (pr.outer == 1 || (((uint64_t)pr.in_o * sizeof(T)) % 16 == 0 &&
                                         ((uint64_t)pr.out_o * sizeof(T)) % 16 == 0));
     std::lock_guard<std::mutex> lock(dev->mu);
-    if (vec && pr.outer == 1 && !scan_knob("HEPH_SCAN_NO_CHUNKED", 0)) {
+    // A line long enough for the chunked kernel takes it; of several lines,
+    // each of at least 128 MiB takes it with one launch per line (a few long
+    // lines would otherwise wait along their look-back chains; below that the
+    // chunked kernel's ~13 us of fixed cost per launch outweighs the gain:
+    // 4 x 2^26 u32 3.5 -> 5.3 TB/s, 16 x 2^24 3.6 -> 3.7, 3 x 7.5 M 3.1 ->
+    // 2.4).  Whether a line qualifies depends only on its length, so either
+    // every line is launched or none is.
+    const bool per_line = pr.outer == 1 || pr.len * sizeof(T) >= kPerLineChunkedBytes;
+    if (vec && per_line && !scan_knob("HEPH_SCAN_NO_CHUNKED", 0)) {
         heph_status st = HEPH_OK;
-        bool launched;
-        const T *ci = in + pr.in_base;
-        T *co = out + pr.out_base;
-        if (reverse)
-            launched = exclusive ? launch_chunked_any<T, OP, true, true>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st)
-                                 : launch_chunked_any<T, OP, true, false>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st);
-        else
-            launched = exclusive ? launch_chunked_any<T, OP, false, true>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st)
-                                 : launch_chunked_any<T, OP, false, false>(dev, stream, ci, co, pr.len, reverse, exclusive, carry, &st);
+        bool launched = false;
+        for (uint64_t line = 0; line < pr.outer; ++line) {
+            const T *ci = in + pr.in_base + (int64_t)line * pr.in_o;
+            T *co = out + pr.out_base + (int64_t)line * pr.out_o;
+            const T *lc = line == 0 ? carry : nullptr;
+            if (reverse)
+                launched = exclusive ? launch_chunked_any<T, OP, true, true>(dev, stream, ci, co, pr.len, reverse, exclusive, lc, &st)
+                                     : launch_chunked_any<T, OP, true, false>(dev, stream, ci, co, pr.len, reverse, exclusive, lc, &st);
+            else
+                launched = exclusive ? launch_chunked_any<T, OP, false, true>(dev, stream, ci, co, pr.len, reverse, exclusive, lc, &st)
+                                     : launch_chunked_any<T, OP, false, false>(dev, stream, ci, co, pr.len, reverse, exclusive, lc, &st);
+            if (!launched || st != HEPH_OK) break;
+        }
         if (launched) return st;
     }
-    const uint64_t tiles_per_line = (pr.len + S::TILE - 1) / S::TILE;
+    // A line shorter than one 32 KiB tile takes 16 KiB tiles (a 16 KiB line
+    // fills its tile instead of idling half the CTA).
+    const bool small_tile = pr.len < (uint64_t)S::TILE;
+    const uint64_t tile_elems = small_tile ? (uint64_t)ScanShape<T, kLookbackVectorsSmall>::TILE : (uint64_t)S::TILE;
+    const uint64_t tiles_per_line = (pr.len + tile_elems - 1) / tile_elems;
     const uint64_t tiles = tiles_per_line * pr.outer;
     if (tiles > 0x7fffffffull) return fail(HEPH_DISPATCH_FAILED, "scan grid too large");
     LookbackParams<T> p{};
@@ -853,6 +965,12 @@ static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *
     p.out = out + pr.out_base;
     p.len = pr.len;
     p.tiles_per_line = tiles_per_line;
+    p.lines = pr.outer;
+    // Position-major numbering pays once a line's prefix chain is long
+    // (measured: 32 tiles per line 4.7 -> 6.4 TB/s); for lines of a few tiles
+    // it only scatters the CTAs in flight over memory (2 tiles: 6.3 -> 5.8).
+    p.interleaved = pr.outer > 1 && tiles_per_line >= kInterleaveMinTiles;
+    p.pos_step = p.interleaved ? pr.outer : 1;
     p.in_line = pr.in_o;
     p.out_line = pr.out_o;
     p.carry = carry;
@@ -861,16 +979,8 @@ static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *
     p.exclusive = exclusive;
     const dim3 grid((unsigned)tiles);
     const int sel = (vec ? 4 : 0) | (reverse ? 2 : 0) | (exclusive ? 1 : 0);
-    switch (sel) {
-        case 0: scan_lookback_kernel<T, OP, false, kLookbackVectors, false, false><<<grid, kScanThreads, 0, stream>>>(p); break;
-        case 1: scan_lookback_kernel<T, OP, false, kLookbackVectors, false, true><<<grid, kScanThreads, 0, stream>>>(p); break;
-        case 2: scan_lookback_kernel<T, OP, false, kLookbackVectors, true, false><<<grid, kScanThreads, 0, stream>>>(p); break;
-        case 3: scan_lookback_kernel<T, OP, false, kLookbackVectors, true, true><<<grid, kScanThreads, 0, stream>>>(p); break;
-        case 4: scan_lookback_kernel<T, OP, true, kLookbackVectors, false, false><<<grid, kScanThreads, 0, stream>>>(p); break;
-        case 5: scan_lookback_kernel<T, OP, true, kLookbackVectors, false, true><<<grid, kScanThreads, 0, stream>>>(p); break;
-        case 6: scan_lookback_kernel<T, OP, true, kLookbackVectors, true, false><<<grid, kScanThreads, 0, stream>>>(p); break;
-        default: scan_lookback_kernel<T, OP, true, kLookbackVectors, true, true><<<grid, kScanThreads, 0, stream>>>(p); break;
-    }
+    if (small_tile) launch_lookback<T, OP, kLookbackVectorsSmall>(sel, grid, stream, p);
+    else launch_lookback<T, OP, kLookbackVectors>(sel, grid, stream, p);
     HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "scan launch");
     return HEPH_OK;
 }
@@ -887,7 +997,9 @@ __global__ void lookback_timeout_selftest_kernel(StatusView status, unsigned int
     LookbackParams<uint32_t> p{};
     p.status = status;
     p.err = err;
-    (void)lookback<uint32_t, OP_SUM>(p, 1, 0, threadIdx.x & 31);
+    p.lines = 1;
+    p.pos_step = 1;
+    (void)lookback<uint32_t, OP_SUM>(p, 1, 1, threadIdx.x & 31);
 }
 
 __global__ void mbar_timeout_selftest_kernel(unsigned int *err) {

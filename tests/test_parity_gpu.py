@@ -245,7 +245,10 @@ def test_scan_prod_and_unaligned(device, oracle, dt):
 def test_scan_2d_both_axes(device, oracle, dt):
     rng = np.random.default_rng(5)
     ops = CudaScanOps()
-    for shape in [(3, 4), (7, 5000), (5000, 7), (3, 20000), (64, 4097), (2, 513)]:
+    # (5, 70001), (4, 65540): lines of 8+ look-back tiles (interleaved numbering), unaligned and aligned
+    # rows; (300, 4096): rows of exactly one 16 KiB tile.
+    for shape in [(3, 4), (7, 5000), (5000, 7), (3, 20000), (64, 4097), (2, 513), (5, 70001), (4, 65540),
+                  (24, 40960), (300, 4096)]:
         x = rand(dt, shape[0] * shape[1], rng)
         buf = device.upload(x)
         for axis in (0, 1):
@@ -291,11 +294,30 @@ def test_repeated_scans_reuse_workspace(device, oracle):
     device.synchronize()  # no device-side error (look-back timeout) was raised
 
 
+@pytest.mark.parametrize("dt,shape", [(np.uint32, (2, 33_554_444)), (np.int64, (2, 16_777_220)),
+                                      (np.uint32, (3, 7_500_000))])
+def test_chunked_scan_multiline(device, oracle, dt, shape):
+    """Several lines of at least 128 MiB take the chunked kernel, one launch
+    per line: each line starts from the identity (no carry leaks from the line
+    before).  (3, 7.5 M) u32 lines qualify for it alone but take look-back."""
+    rng = np.random.default_rng(77)
+    x = rand(dt, shape[0] * shape[1], rng)
+    buf, out = device.upload(x), device.alloc_zeroed(dt, x.size)
+    for rev in (False, True):
+        for exc in (False, True):
+            CudaScanOps().scan_axis_into(CumSumOp, device, StridedView(buf, Layout.c_contiguous(list(shape))), 1,
+                                         int(rev), StridedView(out, Layout.c_contiguous(list(shape))), exclusive=exc)
+            np.testing.assert_array_equal(device.download_owned(out),
+                                          oracle.scan_axis(x, list(shape), 1, reverse=rev, exclusive=exc),
+                                          err_msg=f"rev={rev} exc={exc}")
+
+
 @pytest.fixture
 def small_parts(monkeypatch):
-    """16 KiB parts for the chunked scan, so that a few million elements span
-    many chunks (the launcher reads the knob at every call)."""
-    monkeypatch.setenv("HEPH_SCAN_PART_KB", "16")
+    """One chunked-scan CTA per SM (148 parts of 16 KiB per chunk), so that a
+    few million elements span many chunks and every size below takes the
+    chunked kernel (the launcher reads the knob at every call)."""
+    monkeypatch.setenv("HEPH_SCAN_CHUNK_CTAS", "1")
     yield
 
 
