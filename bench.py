@@ -63,6 +63,10 @@ CONFIGS = {
     7: dict(workload="f32 full sum over the [16384 x 15999] sub-block (row stride 16387, offset 1) of a "
                      "16384 x 16387 matrix, U[-1,1) seed 0; rows not 16-byte aligned",
             rows=16384, cols=15999, ld=16387, offset=1, dtype="f32", kernel="reduce_runs_kernel"),
+    # Axis scan of a matrix (ScanOps::scan_axis_into on a rank-2 view, axis 1):
+    # many long lines, each a look-back chain of 32 tiles.
+    8: dict(workload="u32 inclusive scan along the rows (axis 1) of a [1024 x 262144] row-major matrix, "
+                     "h&15 seed 1", rows=1024, cols=262144, dtype="u32", kernel="scan_lookback_kernel"),
 }
 
 
@@ -219,6 +223,16 @@ def cpu_sample(cfg_id: int, cfg: dict, oracle, seconds: float = 10.0, threads: i
             reps += 1
         return 4 * rows * cols / ((time.perf_counter() - t0) / reps) / 1e9, 1, \
             f"f32 sum of a [1024 x {cols}] sub-block (row stride {ld}) x {reps} reps, one thread"
+    if cfg_id == 8:
+        rows, cols = 32, cfg["cols"]
+        x = oracle.generate(oracle.GEN_U32_LOW4, 1, rows * cols)
+        out = np.empty_like(x)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            oracle.scan_axis(x, [rows, cols], 1, out_storage=out)
+            reps += 1
+        return 8 * rows * cols / ((time.perf_counter() - t0) / reps) / 1e9, 1, \
+            f"u32 row scan of [32 x {cols}] x {reps} reps, one thread"
     rows, cols = 512, cfg["cols"]
     x = oracle.generate(oracle.GEN_F64_UNIT, 3, rows * cols)
     reps, t0 = 0, time.perf_counter()
@@ -542,6 +556,20 @@ def main():
         kernel_bytes = bytes_per_step
         kernel_step = None
         units = rows * cols
+    elif args.config == 8:
+        rows, cols = cfg["rows"], cfg["cols"]
+        x = dev.alloc_uninitialized(np.uint32, rows * cols)
+        S.synth_fill(dev, x, S.SYNTH_U32_LOW4, seed=1, stream=sp)
+        y = dev.alloc_uninitialized(np.uint32, rows * cols)
+        lay = Layout.c_contiguous([rows, cols])
+        ops = H.CudaScanOps()
+
+        def step():
+            ops.scan_axis_into(CumSumOp, dev, StridedView(x, lay), 1, 0, StridedView(y, lay), stream=sp)
+        bytes_per_step = 8 * rows * cols
+        kernel_bytes = bytes_per_step
+        kernel_step = None
+        units = rows * cols
     else:  # config 5: strong scaling of 2^32 i32 over the ranks
         total = cfg["n"]
         n = (total + world - 1) // world
@@ -788,6 +816,19 @@ def run_e2e(args, cfg, dev, stream, sp, world, rank, comm, max_over_ranks, barri
                                  stream=sp)
             check(N.lib.heph_buffer_download_async(dev.handle, out.handle, 0, ho, 1, ctypes.c_void_p(sp)))
         bytes_step, h2d, d2h = 4 * rows * cols, 4 * total, 4
+    elif args.config == 8:
+        rows, cols = cfg["rows"], cfg["cols"]
+        n = rows * cols
+        hin, ho = pinned(4 * n), pinned(4 * n)
+        x, y = dev.alloc_uninitialized(np.uint32, n), dev.alloc_uninitialized(np.uint32, n)
+        lay = Layout.c_contiguous([rows, cols])
+        ops = H.CudaScanOps()
+
+        def e2e_step():
+            check(N.lib.heph_buffer_upload_async(dev.handle, x.handle, 0, hin, n, ctypes.c_void_p(sp)))
+            ops.scan_axis_into(CumSumOp, dev, StridedView(x, lay), 1, 0, StridedView(y, lay), stream=sp)
+            check(N.lib.heph_buffer_download_async(dev.handle, y.handle, 0, ho, n, ctypes.c_void_p(sp)))
+        bytes_step, h2d, d2h = 8 * n, 4 * n, 4 * n
     else:
         rows, cols = cfg["rows"], cfg["cols"]
         hin, ho = pinned(8 * rows * cols), pinned(8 * cols)
