@@ -42,9 +42,9 @@ constexpr uint32_t kPolls = 1u << 20;        // bounded waits on other CTAs
 constexpr int kLookbackVectors = 8;          // look-back tile: 8 x 128-bit per thread (32 KiB)
 constexpr int kLookbackVectorsSmall = 4;     // look-back tile for lines under 32 KiB (16 KiB)
 constexpr uint64_t kInterleaveMinTiles = 8;  // look-back tiles per line from which lines interleave
-constexpr int kChunkVectors = 4;
-constexpr uint64_t kPerLineChunkedBytes = 128ull << 20;  // see launch_scan_typed
-constexpr int kMaxCachedDevices = 64;        // device ordinals with cached launch queries             // chunked kernel tile: 4 x 128-bit per thread (16 KiB)
+constexpr int kChunkVectors = 4;             // chunked kernel tile: 4 x 128-bit per thread (16 KiB)
+constexpr uint64_t kPerLineChunkedBytes = 128ull << 20;  // lines of several that take the chunked kernel
+constexpr int kMaxCachedDevices = 64;        // device ordinals with cached launch queries
 constexpr int kChunkMaxBuffers = 6;          // part buffers per CTA of the chunked scan
 constexpr int kChunkMaxPartsPerThread = 2;   // chunked grids have at most 2 x 256 CTAs
 
