@@ -41,7 +41,7 @@ constexpr int kScanWarps = kScanThreads / 32;
 constexpr uint32_t kPolls = 1u << 20;        // bounded waits on other CTAs
 constexpr int kLookbackVectors = 8;          // look-back tile: 8 x 128-bit per thread (32 KiB)
 constexpr int kLookbackVectorsSmall = 4;     // look-back tile for lines under 32 KiB (16 KiB)
-constexpr uint64_t kInterleaveMinTiles = 8;  // look-back tiles per line from which lines interleave
+constexpr uint64_t kInterleaveMinTiles = 2;  // look-back tiles per line from which lines interleave
 constexpr int kChunkVectors = 4;             // chunked kernel tile: 4 x 128-bit per thread (16 KiB)
 constexpr uint64_t kPerLineChunkedBytes = 128ull << 20;  // lines of several that take the chunked kernel
 constexpr int kMaxCachedDevices = 64;        // device ordinals with cached launch queries
@@ -417,11 +417,10 @@ __device__ T lookback(const LookbackParams<T> &p, uint64_t tile, uint64_t pos, i
     }
 }
 
-// One tile per CTA.  Long lines are numbered position-major (the first tile
-// of every line, then the second, ...) so the resident CTAs advance all
-// lines' prefix chains at once instead of waiting along one line's chain;
-// short lines stay line-major, which keeps the CTAs in flight on one
-// contiguous stretch of memory.
+// One tile per CTA.  Lines of several tiles are numbered position-major (the
+// first tile of every line, then the second, ...) so the resident CTAs
+// advance all lines' prefix chains at once instead of waiting along one
+// line's chain.
 template <typename T, int OP, bool VEC, int JV, bool REV, bool EXCL>
 __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const LookbackParams<T> p) {
     using S = ScanShape<T, JV>;
@@ -966,10 +965,11 @@ static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *
     p.len = pr.len;
     p.tiles_per_line = tiles_per_line;
     p.lines = pr.outer;
-    // Position-major numbering pays once a line's prefix chain is long
-    // (measured: 32 tiles per line 4.7 -> 6.4 TB/s); for lines of a few tiles
-    // it only scatters the CTAs in flight over memory (2 tiles: 6.3 -> 5.8).
-    p.interleaved = pr.outer > 1 && tiles_per_line >= kInterleaveMinTiles;
+    // Position-major numbering measured faster at every line length (u32,
+    // 1 GiB, line-major -> position-major TB/s: 2 tiles per line 6.5 -> 6.8,
+    // 8 tiles 5.4 -> 6.7, 64 tiles 4.3 -> 6.7, 256 tiles 3.9 -> 5.2).
+    p.interleaved = pr.outer > 1 &&
+                    tiles_per_line >= (uint64_t)scan_knob("HEPH_SCAN_INTERLEAVE_MIN", (int)kInterleaveMinTiles);
     p.pos_step = p.interleaved ? pr.outer : 1;
     p.in_line = pr.in_o;
     p.out_line = pr.out_o;

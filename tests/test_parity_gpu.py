@@ -245,7 +245,7 @@ def test_scan_prod_and_unaligned(device, oracle, dt):
 def test_scan_2d_both_axes(device, oracle, dt):
     rng = np.random.default_rng(5)
     ops = CudaScanOps()
-    # (5, 70001), (4, 65540): lines of 8+ look-back tiles (interleaved numbering), unaligned and aligned
+    # (5, 70001), (4, 65540): lines of 9 look-back tiles (position-major numbering), unaligned and aligned
     # rows; (300, 4096): rows of exactly one 16 KiB tile.
     for shape in [(3, 4), (7, 5000), (5000, 7), (3, 20000), (64, 4097), (2, 513), (5, 70001), (4, 65540),
                   (24, 40960), (300, 4096)]:
