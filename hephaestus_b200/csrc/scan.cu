@@ -43,6 +43,8 @@ constexpr int kLookbackVectors = 8;          // look-back tile: 8 x 128-bit per 
 constexpr int kLookbackVectorsSmall = 4;     // look-back tile for lines under 32 KiB (16 KiB)
 constexpr uint64_t kInterleaveMinTiles = 2;  // look-back tiles per line from which lines interleave
 constexpr int kChunkVectors = 4;             // chunked kernel tile: 4 x 128-bit per thread (16 KiB)
+constexpr uint64_t kTwoPassMinTiles = 640;              // single lines of 640+ look-back tiles ...
+constexpr uint64_t kTwoPassMaxBytes = 64ull << 20;      // ... and at most 64 MiB take the two-pass scan
 constexpr uint64_t kPerLineChunkedBytes = 128ull << 20;  // lines of several that take the chunked kernel
 constexpr int kMaxCachedDevices = 64;        // device ordinals with cached launch queries
 constexpr int kChunkMaxBuffers = 6;          // part buffers per CTA of the chunked scan
@@ -470,6 +472,74 @@ __global__ void __launch_bounds__(kScanThreads) scan_lookback_kernel(const Lookb
     tile_outputs<T, OP, JV, REV, EXCL>(x, r, s_prefix, y);
     if (VEC && !full) store_tile_partial_vec<T, JV>(lout + start, valid, base, y);
     else store_tile<T, JV>(lout + start, valid, full, base, y);
+}
+
+// ------------------------------------------ two-pass scan of a mid-size line
+//
+// A single line too short for the chunked kernel but long enough that a
+// look-back chain would dominate (its inclusive-prefix front advances 32
+// tiles per status round trip): pass 1 writes every tile's total, pass 2
+// folds, per tile, the totals before it (in scan order) and scans the tile
+// with that prefix.  The line is at most a few tens of MB, so pass 2 reads
+// it back from L2.
+
+// Tile `blockIdx.x` of the line into x (identity past the end).
+template <typename T, int OP, bool VEC, int JV>
+__device__ __forceinline__ void load_line_tile(const T *in, uint64_t len, int base, T (&x)[JV][ScanShape<T, JV>::V],
+                                               uint64_t &start, uint64_t &valid) {
+    constexpr int TILE = ScanShape<T, JV>::TILE;
+    start = (uint64_t)blockIdx.x * TILE;
+    valid = min((uint64_t)TILE, len - start);
+    if (VEC && valid == (uint64_t)TILE) load_tile_vec<T, JV>(in + start, base, x, false);
+    else if (VEC) load_tile_partial_vec<T, OP, JV>(in + start, valid, base, x);
+    else load_tile_scalar<T, OP, JV>(in + start, valid, base, x);
+}
+
+template <typename T, int OP, bool VEC, int JV>
+__global__ void __launch_bounds__(kScanThreads) scan_tile_totals_kernel(const T *__restrict__ in, uint64_t len,
+                                                                       T *__restrict__ totals) {
+    constexpr int V = ScanShape<T, JV>::V;
+    __shared__ T scratch[kScanWarps];
+    const int base = tile_base_pos<T, JV>(threadIdx.x >> 5, threadIdx.x & 31);
+    T x[JV][V];
+    uint64_t start, valid;
+    load_line_tile<T, OP, VEC, JV>(in, len, base, x, start, valid);
+    T acc = identity<T, OP>();
+#pragma unroll
+    for (int j = 0; j < JV; ++j)
+#pragma unroll
+        for (int c = 0; c < V; ++c) acc = combine<T, OP>(acc, x[j][c]);
+    acc = block_fold<T, OP, kScanThreads>(acc, scratch);
+    if (threadIdx.x == 0) totals[blockIdx.x] = acc;
+}
+
+template <typename T, int OP, bool VEC, int JV, bool REV, bool EXCL>
+__global__ void __launch_bounds__(kScanThreads) scan_tile_apply_kernel(const T *__restrict__ in, T *__restrict__ out,
+                                                                      uint64_t len, uint64_t ntiles,
+                                                                      const T *__restrict__ totals,
+                                                                      const T *__restrict__ carry) {
+    constexpr int V = ScanShape<T, JV>::V;
+    __shared__ T s_warp[kScanWarps];
+    __shared__ T scratch[kScanWarps];
+    const int base = tile_base_pos<T, JV>(threadIdx.x >> 5, threadIdx.x & 31);
+    T x[JV][V];
+    uint64_t start, valid;
+    load_line_tile<T, OP, VEC, JV>(in, len, base, x, start, valid);  // in flight during the fold below
+    // The fold of the totals before this tile in scan order (after it, for a
+    // reverse scan), seeded with the carry.
+    const uint64_t k = blockIdx.x;
+    const uint64_t lo = REV ? k + 1 : 0, hi = REV ? ntiles : k;
+    T pre = identity<T, OP>();
+    for (uint64_t i = lo + threadIdx.x; i < hi; i += kScanThreads) pre = combine<T, OP>(pre, totals[i]);
+    pre = block_fold<T, OP, kScanThreads>(pre, scratch);
+    if (carry) pre = combine<T, OP>(*carry, pre);
+    TileScan<T, JV> r;
+    tile_local_scan<T, OP, JV, REV>(x, s_warp, r);
+    T y[JV][V];
+    tile_outputs<T, OP, JV, REV, EXCL>(x, r, pre, y);
+    if (valid == (uint64_t)ScanShape<T, JV>::TILE && VEC) store_tile<T, JV>(out + start, valid, true, base, y);
+    else if (VEC) store_tile_partial_vec<T, JV>(out + start, valid, base, y);
+    else store_tile<T, JV>(out + start, valid, false, base, y);
 }
 
 // --------------------------------- chunked reduce-then-scan, parts in smem
@@ -907,6 +977,38 @@ static void launch_lookback(int sel, dim3 grid, cudaStream_t stream, const Lookb
     }
 }
 
+// Both passes of the two-pass scan on `stream`; the tile totals live in the
+// stream's workspace.  The caller holds the device's lock.
+template <typename T, int OP>
+static heph_status launch_two_pass(Device *dev, cudaStream_t stream, const T *in, T *out, uint64_t len,
+                                   uint64_t ntiles, bool vec, bool reverse, bool exclusive, const T *carry) {
+    Workspace *ws = nullptr;
+    heph_status st = workspace_for(dev, stream, (size_t)ntiles * sizeof(T), 0, &ws);
+    if (st != HEPH_OK) return st;
+    T *totals = static_cast<T *>(ws->partials);
+    constexpr int JV = kLookbackVectors;
+    const dim3 grid((unsigned)ntiles);
+    if (vec) scan_tile_totals_kernel<T, OP, true, JV><<<grid, kScanThreads, 0, stream>>>(in, len, totals);
+    else scan_tile_totals_kernel<T, OP, false, JV><<<grid, kScanThreads, 0, stream>>>(in, len, totals);
+    HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "scan tile totals launch");
+    const int sel = (vec ? 4 : 0) | (reverse ? 2 : 0) | (exclusive ? 1 : 0);
+    switch (sel) {
+#define HEPH_APPLY(V_, R_, E_) \
+    scan_tile_apply_kernel<T, OP, V_, JV, R_, E_><<<grid, kScanThreads, 0, stream>>>(in, out, len, ntiles, totals, carry)
+        case 0: HEPH_APPLY(false, false, false); break;
+        case 1: HEPH_APPLY(false, false, true); break;
+        case 2: HEPH_APPLY(false, true, false); break;
+        case 3: HEPH_APPLY(false, true, true); break;
+        case 4: HEPH_APPLY(true, false, false); break;
+        case 5: HEPH_APPLY(true, false, true); break;
+        case 6: HEPH_APPLY(true, true, false); break;
+        default: HEPH_APPLY(true, true, true); break;
+#undef HEPH_APPLY
+    }
+    HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "scan apply launch");
+    return HEPH_OK;
+}
+
 template <typename T, int OP>
 static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *in, T *out, const AxisProblem &pr,
                                      bool reverse, bool exclusive, const T *carry) {
@@ -949,6 +1051,18 @@ static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *
             if (!launched || st != HEPH_OK) break;
         }
         if (launched) return st;
+    }
+    // A single line of 640+ tiles below the chunked kernel's minimum: the
+    // two-pass scan (see scan_tile_totals_kernel).  Measured per call, u32,
+    // look-back -> two-pass: 6.3 M elements 18.3 -> 16.0 us, 7 M 19.1 ->
+    // 15.4 us; below ~5 M the second launch costs more than the chain saves
+    // (4.2 M 13.8 -> 15.7 us).
+    if (pr.outer == 1) {
+        const uint64_t nt = (pr.len + S::TILE - 1) / S::TILE;
+        if (nt >= kTwoPassMinTiles && pr.len * sizeof(T) <= kTwoPassMaxBytes &&
+            !scan_knob("HEPH_SCAN_NO_TWO_PASS", 0))
+            return launch_two_pass<T, OP>(dev, stream, in + pr.in_base, out + pr.out_base, pr.len, nt, vec, reverse,
+                                          exclusive, carry);
     }
     // A line shorter than one 32 KiB tile takes 16 KiB tiles (a 16 KiB line
     // fills its tile instead of idling half the CTA).

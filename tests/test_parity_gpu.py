@@ -294,6 +294,26 @@ def test_repeated_scans_reuse_workspace(device, oracle):
     device.synchronize()  # no device-side error (look-back timeout) was raised
 
 
+@pytest.mark.parametrize("dt", DTYPES)
+def test_scan_two_pass_lines(device, oracle, dt):
+    """Single lines of 640+ look-back tiles below the chunked kernel's minimum
+    take the two-pass scan (tile totals, then each tile scanned with the fold
+    of the totals before it): 6 M 4-byte elements, 2.8-2.9 M 8-byte ones;
+    aligned and misaligned views, both directions, inclusive and exclusive."""
+    rng = np.random.default_rng(91 + DTYPES.index(dt))
+    ops = CudaScanOps()
+    for n, off in [(6_000_001, 0), (2_800_003, 0), (2_900_001, 1), (5_500_000, 3)]:
+        x = rand(dt, n + off, rng)
+        buf = device.upload(x)
+        for rev in (False, True):
+            for exc in (False, True):
+                out = device.alloc_zeroed(dt, n)
+                ops.scan_axis_into(CumSumOp, device, StridedView(buf, Layout.try_new([n], [1], off)), 0, int(rev),
+                                   StridedView(out, Layout.c_contiguous([n])), exclusive=exc)
+                want = oracle.scan_axis(x, [n], 0, reverse=rev, exclusive=exc, in_offset=off)
+                assert_close(device.download_owned(out), want[:n], dt, x[off:])
+
+
 @pytest.mark.parametrize("dt,shape", [(np.uint32, (2, 33_554_444)), (np.int64, (2, 16_777_220)),
                                       (np.uint32, (3, 7_500_000))])
 def test_chunked_scan_multiline(device, oracle, dt, shape):
