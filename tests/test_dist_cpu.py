@@ -22,7 +22,9 @@ def _free_port():
     return port
 
 
-def _init(rank, world, port, timeout_s=30):
+def _init(rank, world, port, timeout_s=120):
+    # Generous: spawned ranks import torch at very different speeds on a
+    # loaded machine, and the rendezvous waits for the slowest.
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world,
@@ -64,12 +66,15 @@ def test_partitioned_scan_rank_logic(tmp_path, exclusive, world):
 
 def _failing_worker(rank, world, port, result_dir):
     import torch
-    _init(rank, world, port, timeout_s=5)
+    _init(rank, world, port)
+    # The exchange runs in a group with a short deadline; the rendezvous
+    # above does not, so a slow start is not mistaken for the lost rank.
+    group = dist.new_group(list(range(world)), timeout=datetime.timedelta(seconds=5))
     if rank == 1:
         raise SystemExit(3)  # this rank drops out before the exchange
     try:
         out = [torch.zeros(1) for _ in range(world)]
-        dist.all_gather(out, torch.ones(1))
+        dist.all_gather(out, torch.ones(1), group=group)
         status = "completed"
     except Exception as e:  # noqa: BLE001 - any error is the expected outcome
         status = "error: " + type(e).__name__
