@@ -75,3 +75,34 @@ def test_threads_on_separate_streams(device, oracle):
     assert not any(th.is_alive() for th in threads), "a worker thread did not finish"
     assert not errors, "\n".join(errors)
     device.synchronize()
+
+
+def test_concurrent_device_acquisition(oracle):
+    """Sixteen threads open the same ordinal at once (the reference's
+    concurrency test does the same for CudaDevice acquisition) and each runs a
+    reduction through its own handle."""
+    from hephaestus_b200 import CudaDevice
+
+    x = oracle.generate(oracle.GEN_U32_LOW4, 5, 100_003)
+    want = int(x.astype(np.uint64).sum() & 0xffffffff)
+    got, errors = [None] * 16, []
+    start = threading.Barrier(16)
+
+    def run(t):
+        try:
+            start.wait()
+            dev = CudaDevice(0)
+            buf, out = dev.upload(x), dev.alloc_zeroed(np.uint32, 1)
+            CudaFullReductionOps().reduce_full_into(SumOp, dev, StridedView(buf, Layout.c_contiguous([x.size])),
+                                                    StridedView(out, Layout.c_contiguous([1])))
+            got[t] = int(dev.download_owned(out)[0])
+        except Exception as e:  # noqa: BLE001 - reported below with the thread id
+            errors.append(f"thread {t}: {type(e).__name__}: {e}")
+
+    threads = [threading.Thread(target=run, args=(t,)) for t in range(16)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join(timeout=300)
+    assert not errors, "\n".join(errors)
+    assert got == [want] * 16
