@@ -24,7 +24,9 @@
 
 #include <cstring>
 #include <mutex>
+#include <thread>
 
+#include "comm_wait.h"
 #include "common.cuh"
 #include "kernels.h"
 #include "plan.h"
@@ -210,6 +212,61 @@ extern "C" heph_status heph_comm_abort(heph_comm *comm) {
         comm->aborted = true;
     }
     return HEPH_OK;
+}
+
+extern "C" heph_status heph_comm_wait(heph_comm *comm, heph_stream stream, uint32_t timeout_ms) {
+    if (!comm) return fail(HEPH_INVALID_CONFIGURATION, "null communicator");
+    if (comm->aborted) return fail(HEPH_DISPATCH_FAILED, "communicator was aborted");
+    heph_status st = bind(comm->device);
+    if (st != HEPH_OK) return st;
+    cudaStream_t s = resolve_stream(comm->device, stream);
+    NcclApi &api = nccl();
+    cudaError_t stream_err = cudaSuccess;
+    const CommWaitResult r = comm_wait_policy(
+        timeout_ms,
+        [&] {
+            const cudaError_t e = cudaStreamQuery(s);
+            if (e == cudaSuccess) return StreamPoll::Done;
+            if (e == cudaErrorNotReady) return StreamPoll::Pending;
+            stream_err = e;
+            return StreamPoll::Failed;
+        },
+        [&] {
+            ncclResult_t async = ncclSuccess;
+            if (api.CommGetAsyncError(comm->nccl, &async) != ncclSuccess) return CommPoll::Failed;
+            return (async == ncclSuccess || async == ncclInProgress) ? CommPoll::Ok : CommPoll::Failed;
+        },
+        [&] {
+            api.CommAbort(comm->nccl);
+            comm->aborted = true;
+        },
+        steady_ms, [] { std::this_thread::sleep_for(std::chrono::microseconds(50)); });
+    if (r.ok) return HEPH_OK;
+    if (stream_err != cudaSuccess) return cuda_fail(HEPH_DISPATCH_FAILED, stream_err, r.message.c_str());
+    return fail(HEPH_DISPATCH_FAILED, r.message);
+}
+
+// Runs comm_wait_policy against scripted fakes (no GPU, no NCCL): 0 = the
+// stream completes on its third poll; 1 = NCCL reports an asynchronous error
+// while the stream is pending; 2 = the stream never completes (deadline);
+// 3 = the stream fails.  *out_aborted tells how often the policy aborted.
+extern "C" heph_status heph_selftest_comm_wait_policy(int scenario, uint32_t timeout_ms, int *out_aborted) {
+    if (scenario < 0 || scenario > 3 || !out_aborted) return fail(HEPH_INVALID_CONFIGURATION, "bad self-test argument");
+    int polls = 0, aborts = 0;
+    uint64_t clock = 0;
+    const CommWaitResult r = comm_wait_policy(
+        timeout_ms,
+        [&] {
+            ++polls;
+            if (scenario == 0 && polls >= 3) return StreamPoll::Done;
+            if (scenario == 3) return StreamPoll::Failed;
+            return StreamPoll::Pending;
+        },
+        [&] { return scenario == 1 && polls >= 2 ? CommPoll::Failed : CommPoll::Ok; },
+        [&] { ++aborts; }, [&] { return clock; }, [&] { clock += 1; });
+    *out_aborted = aborts;
+    if (r.ok) return HEPH_OK;
+    return fail(HEPH_DISPATCH_FAILED, r.message);
 }
 
 static heph_status partitioned_args(heph_comm *comm, const heph_buffer *in, const heph_layout *il,

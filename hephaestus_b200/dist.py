@@ -68,6 +68,14 @@ class Communicator:
                                                  reduce_output.buffer.handle, ctypes.byref(rl),
                                                  ctypes.c_void_p(stream) if stream else None))
 
+    def wait(self, timeout_s: float, stream=None):
+        """Host-side deadline on the calls queued on `stream` (heph_comm_wait):
+        returns once they finished; raises HephaestusError (DispatchFailed)
+        after aborting the communicator when NCCL reports an error or the
+        deadline passes first (a peer rank died or never arrived)."""
+        check(N.lib.heph_comm_wait(self._h, ctypes.c_void_p(stream) if stream else None,
+                                   max(1, int(timeout_s * 1000))))
+
     def abort(self):
         if self._h:
             N.lib.heph_comm_abort(self._h)

@@ -348,6 +348,23 @@ heph_status heph_comm_destroy(heph_comm *comm);
 /* Aborts in-flight NCCL work (failure path: a peer is gone). */
 heph_status heph_comm_abort(heph_comm *comm);
 
+/* [EXT] Host-side deadline on a partitioned call: waits until `stream` (NULL
+ * = the device's stream) has finished the work queued on it, polling NCCL's
+ * asynchronous error (ncclCommGetAsyncError) meanwhile.  When NCCL reports an
+ * error, or `timeout_ms` passes first (a peer rank died or never arrived),
+ * the communicator is aborted (ncclCommAbort: its kernels exit) and
+ * DispatchFailed is returned with the reason; the communicator then only
+ * accepts heph_comm_destroy.  The reference has no multi-GPU path and no
+ * counterpart. */
+heph_status heph_comm_wait(heph_comm *comm, heph_stream stream, uint32_t timeout_ms);
+
+/* [EXT] Runs the wait policy of heph_comm_wait against scripted fakes, with
+ * no GPU and no NCCL (0: the stream completes; 1: NCCL reports an error;
+ * 2: the deadline passes; 3: the stream fails); *out_aborted = how many
+ * times the policy aborted the fake communicator.  For tests and health
+ * checks; no counterpart in the reference. */
+heph_status heph_selftest_comm_wait_policy(int scenario, uint32_t timeout_ms, int *out_aborted);
+
 /* Each rank holds one contiguous slice of a global 1-D buffer (rank order =
  * slice order).  `out` (one element, dtype may widen I32->I64 / F32->F64)
  * receives the reduction of the WHOLE global buffer on every rank: local

@@ -104,3 +104,25 @@ def test_carries_rule():
     np.testing.assert_array_equal(carries([3, 4, 5], dtype=np.int64), [0, 3, 7])
     np.testing.assert_array_equal(carries([2, 3, 4], N.PROD, dtype=np.int64), [1, 2, 6])
     np.testing.assert_array_equal(carries([2**31 - 1, 1, 1], dtype=np.int32), [0, 2**31 - 1, -2**31])
+
+
+@pytest.mark.parametrize("scenario,ok,aborted,words", [
+    (0, True, 0, ""),
+    (1, False, 1, "asynchronous error"),
+    (2, False, 1, "deadline of 50 ms expired"),
+    (3, False, 0, "stream of the partitioned call failed"),
+])
+def test_comm_wait_policy(scenario, ok, aborted, words):
+    """The host-side deadline of heph_comm_wait, run against scripted fakes of
+    the stream and of NCCL (no GPU): it returns when the stream completes,
+    aborts the communicator on an NCCL error or an expired deadline, and only
+    reports a failed stream."""
+    import ctypes
+    from hephaestus_b200 import _native as N
+    n = ctypes.c_int(-1)
+    st = N.lib.heph_selftest_comm_wait_policy(scenario, 50, ctypes.byref(n))
+    assert (st == 0) == ok
+    assert n.value == aborted
+    if not ok:
+        assert st == N.DISPATCH_FAILED
+        assert words in N.lib.heph_last_error().decode()
