@@ -76,7 +76,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=5)
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end measurement")
     ap.add_argument("--published", action="store_true",
                     help="time the reference's own published reduce/scan cases (benchmark_results.md) instead")
@@ -86,6 +86,8 @@ def parse():
                     help="configs 3/4: the same-shape view at element offset K of a row-padded matrix "
                          "(rows not 16-byte aligned)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-check", action="store_true",
+                    help="config 5: skip the element-by-element check of the results after the timed region")
     ap.add_argument("--n", type=int, default=None,
                     help="override the element count of configs 1, 2 and 5 (small profiling cases)")
     return ap.parse_args()
@@ -175,72 +177,80 @@ class ClockSampler:
 # --------------------------------------------------------------- reference arm
 
 
-def cpu_sample(cfg_id: int, cfg: dict, oracle, seconds: float = 10.0, threads: int = 0):
-    """Time the oracle's multithreaded restatement on a bounded sample.
-    Returns (GB/s, cores, sample description).  threads=0 means every host
-    core this process may run on: the count is passed to the oracle
-    explicitly, so torchrun's OMP_NUM_THREADS=1 does not shrink the sample."""
-    threads = threads or len(os.sched_getaffinity(0))
-    cores = threads
-    if cfg_id == 2 or cfg_id == 5:
-        n = 1 << 26
+_CPU_DATA = {}
+
+
+def cpu_workload(cfg_id: int, cfg: dict, oracle, threads: int):
+    """The configured workload at its full size on the host: (one pass, its
+    algorithmic bytes, description).  Inputs are generated once per process
+    by the oracle's generator (the device's SplitMix64 stream)."""
+    mt = f"{threads} threads" if threads > 1 else "one thread"
+
+    def data(key, make):
+        if key not in _CPU_DATA:
+            _CPU_DATA[key] = make()
+        return _CPU_DATA[key]
+
+    if cfg_id in (2, 5):
+        n = cfg["n"]
         dt = np.uint32 if cfg_id == 2 else np.int32
         kind = oracle.GEN_U32_LOW4 if cfg_id == 2 else oracle.GEN_I32_PM1000
-        x = oracle.generate(kind, 1 if cfg_id == 2 else 4, n)
-        out = np.empty_like(x)
-        fn = (oracle.exclusive_scan_u32_mt if cfg_id == 2 else oracle.inclusive_scan_i32_mt)
-        fn(x, out, 0, threads)
-        reps, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            fn(x, out, 0, threads)
-            reps += 1
-        dt_s = (time.perf_counter() - t0) / reps
-        return 8 * n / dt_s / 1e9, cores, f"{'exclusive u32' if cfg_id == 2 else 'inclusive i32'} " \
-                                          f"scan of 2^26 elements x {reps} reps"
+        x = data(("x", cfg_id, n), lambda: oracle.generate(kind, 1 if cfg_id == 2 else 4, n))
+        out = data(("y", cfg_id, n), lambda: np.empty(n, dt))
+        if cfg_id == 2:
+            return (lambda: oracle.exclusive_scan_u32_mt(x, out, 0, threads)), 8 * n, \
+                f"u32 exclusive scan of {n} elements ({mt})"
+
+        def step5():
+            oracle.inclusive_scan_i32_mt(x, out, 0, threads)
+            oracle.sum_i32_to_i64_mt(x, threads)
+        return step5, 12 * n, f"i32 inclusive scan + i64 sum of {n} elements ({mt})"
     if cfg_id == 1:
         n = cfg["n"]
-        x = oracle.generate(oracle.GEN_F32_UNIFORM_PM1, 0, n)
-        reps, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            oracle.sum_f32_mt(x, threads)
-            reps += 1
-        return 4 * n / ((time.perf_counter() - t0) / reps) / 1e9, cores, f"f32 sum of 2^20 x {reps} reps"
+        x = data(("x", 1, n), lambda: oracle.generate(oracle.GEN_F32_UNIFORM_PM1, 0, n))
+        return (lambda: oracle.sum_f32_mt(x, threads)), 4 * n, f"f32 sum of {n} elements ({mt})"
     if cfg_id == 3:
-        rows, cols = 8192, cfg["cols"]
-        x = oracle.generate(oracle.GEN_F32_NORMAL, 2, rows * cols)
-        reps, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            oracle.row_argmax_f32_mt(x, rows, cols, threads)
-            reps += 1
-        return (4 * rows * cols + 8 * rows) / ((time.perf_counter() - t0) / reps) / 1e9, cores, \
-            f"row max+argmax of [8192 x 4096] x {reps} reps"
+        rows, cols = cfg["rows"], cfg["cols"]
+        x = data(("x", 3), lambda: oracle.generate(oracle.GEN_F32_NORMAL, 2, rows * cols))
+        return (lambda: oracle.row_argmax_f32_mt(x, rows, cols, threads)), 4 * rows * cols + 8 * rows, \
+            f"row max + argmax of [{rows} x {cols}] f32 ({mt})"
+    if cfg_id == 4:
+        rows, cols = cfg["rows"], cfg["cols"]
+        x = data(("x", 4), lambda: oracle.generate(oracle.GEN_F64_UNIT, 3, rows * cols))
+        return (lambda: oracle.col_sum_f64_mt(x, rows, cols, threads)), 8 * rows * cols + 8 * cols, \
+            f"column sum of [{rows} x {cols}] f64 ({mt})"
     if cfg_id in (6, 7):
-        rows, cols, ld, off = 1024, cfg["cols"], cfg["ld"], cfg["offset"]
-        x = oracle.generate(oracle.GEN_F32_UNIFORM_PM1, 0, rows * ld + off)
-        reps, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            oracle.reduce_full(x, [rows, cols], [ld, 1], off)
-            reps += 1
-        return 4 * rows * cols / ((time.perf_counter() - t0) / reps) / 1e9, 1, \
-            f"f32 sum of a [1024 x {cols}] sub-block (row stride {ld}) x {reps} reps, one thread"
-    if cfg_id == 8:
-        rows, cols = 32, cfg["cols"]
-        x = oracle.generate(oracle.GEN_U32_LOW4, 1, rows * cols)
-        out = np.empty_like(x)
-        reps, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            oracle.scan_axis(x, [rows, cols], 1, out_storage=out)
-            reps += 1
-        return 8 * rows * cols / ((time.perf_counter() - t0) / reps) / 1e9, 1, \
-            f"u32 row scan of [32 x {cols}] x {reps} reps, one thread"
-    rows, cols = 512, cfg["cols"]
-    x = oracle.generate(oracle.GEN_F64_UNIT, 3, rows * cols)
+        rows, cols, ld, off = cfg["rows"], cfg["cols"], cfg["ld"], cfg["offset"]
+        x = data(("x", cfg_id), lambda: oracle.generate(oracle.GEN_F32_UNIFORM_PM1, 0, rows * ld + off))
+        return (lambda: oracle.reduce_full(x, [rows, cols], [ld, 1], off)), 4 * rows * cols, \
+            f"f32 sum of the [{rows} x {cols}] sub-block (row stride {ld}) (one thread: sequential strided fold)"
+    rows, cols = cfg["rows"], cfg["cols"]  # config 8
+    x = data(("x", 8), lambda: oracle.generate(oracle.GEN_U32_LOW4, 1, rows * cols))
+    out = data(("y", 8), lambda: np.empty_like(x))
+    return (lambda: oracle.scan_axis(x, [rows, cols], 1, out_storage=out)), 8 * rows * cols, \
+        f"u32 row scan of [{rows} x {cols}] (one thread: sequential per-line fold)"
+
+
+def cpu_threads_used(cfg_id: int, threads: int) -> int:
+    return 1 if cfg_id in (6, 7, 8) else threads
+
+
+def cpu_sample(cfg_id: int, cfg: dict, oracle, seconds: float = 10.0, threads: int = 0):
+    """Time the oracle restatement on the FULL configured workload, repeated
+    until `seconds` have passed (at least one pass).  Returns (GB/s, cores,
+    description).  threads=0 means every host core this process may run on:
+    the count is passed to the oracle explicitly, so torchrun's
+    OMP_NUM_THREADS=1 does not shrink the sample."""
+    threads = threads or len(os.sched_getaffinity(0))
+    fn, nbytes, desc = cpu_workload(cfg_id, cfg, oracle, threads)
     reps, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < seconds:
-        oracle.col_sum_f64_mt(x, rows, cols, threads)
+    while True:
+        fn()
         reps += 1
-    return (8 * rows * cols + 8 * cols) / ((time.perf_counter() - t0) / reps) / 1e9, cores, \
-        f"column sum of [512 x 65536] f64 x {reps} reps"
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt_s = (time.perf_counter() - t0) / reps
+    return nbytes / dt_s / 1e9, cpu_threads_used(cfg_id, threads), f"{desc} x {reps} passes"
 
 
 def cpu_model() -> str:
@@ -255,40 +265,106 @@ def cpu_model() -> str:
 
 
 def run_reference(args, cfg):
+    """The reference arm: the oracle restatement of the reference's host
+    device timed on this box's cores, on the same configured workload and
+    with the same `config` as the GPU arm.  Rank 0 alone runs under torchrun.
+    Each step is one or more full passes over the workload (at least ~1 s);
+    `value` uses every host core, and the single-threaded figure -- the
+    reference's host device is single-threaded -- is reported beside it as
+    `single_thread_value`."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     sys.path.insert(0, ROOT)
     from oracle import host_ref as oracle
     oracle.build()
-    per_step = max(1.0, min(6.0, 120.0 / max(1, args.steps + args.warmup)))
+    shrink = cpu_fit(args.config, cfg)
+    if shrink:
+        cfg = dict(cfg, n=shrink)
     vals = []
     desc, cores = "", 0
+    t_run = time.perf_counter()
+    steps_run = 0
     for i in range(args.warmup + args.steps):
-        v, cores, desc = cpu_sample(args.config, cfg, oracle, seconds=per_step)
+        v, cores, desc = cpu_sample(args.config, cfg, oracle, seconds=1.0)
         if i >= args.warmup:
             vals.append(v)
+            steps_run += 1
+        # keep the whole arm within a few minutes on slow hosts
+        if time.perf_counter() - t_run > 240 and vals:
+            break
     value = statistics.median(vals)
-    # The reference's host device is single-threaded ("never a performance
-    # path"): that figure is reported beside the all-cores one.
-    single, _, single_desc = (value, cores, desc) if cores == 1 else \
-        cpu_sample(args.config, cfg, oracle, seconds=min(per_step, 5.0), threads=1)
+    if cores == 1:
+        single, single_desc = value, desc
+    else:
+        single, _, single_desc = cpu_sample(args.config, cfg, oracle, seconds=0.0, threads=1)
+    sample = desc + " per step (oracle restatement of the host reference semantics)"
+    if shrink:
+        sample += f"; host memory allows {shrink} of the {CONFIGS[args.config]['n']} elements"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "higher_is_better": True, "scaling": "weak" if args.config != 5 else "strong",
+        "n_gpus": world, "steps": args.steps, "steps_run": steps_run, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": scaling_kind(args.config),
         "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
-        "config": {"workload": cfg["workload"], "config_index": args.config},
+        "config": config_dict(args, cfg, world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": desc + " per step (oracle restatement of the host reference semantics, "
-                                          + ("OpenMP over all cores)" if cores > 1 else "sequential strided fold)"),
+                         "sample": sample,
                          "single_thread_value": round(single, 3), "single_thread_sample": single_desc,
+                         "primary": "single_thread_value (the reference's host device is single-threaded)",
                          "nproc": os.cpu_count(), "cpu_model": cpu_model()},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def cpu_fit(cfg_id: int, cfg: dict):
+    """Config 5 holds 2 x 16 GiB on the host.  Returns None when the host has
+    room for it (with 8 GiB to spare), else the largest power-of-two element
+    count that fits."""
+    if cfg_id != 5:
+        return None
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except Exception:
+        return None
+    need = 8 * cfg["n"] + (8 << 30)
+    if avail >= need:
+        return None
+    n = 1 << 26
+    while 8 * (2 * n) + (8 << 30) <= avail and 2 * n < cfg["n"]:
+        n *= 2
+    return n
+
+
+def scaling_kind(cfg_id: int) -> str:
+    return "strong" if cfg_id == 5 else "weak"
+
+
+def config_dict(args, cfg: dict, world: int) -> dict:
+    """The `config` object, identical in both arms for the same flags."""
+    if cfg.get("n") is not None and args.config == 5:
+        per = (cfg["n"] + world - 1) // world
+        total = cfg["n"]
+    elif cfg.get("n") is not None:
+        per = cfg["n"]
+        total = per * world
+    else:
+        per = cfg["rows"] * cfg["cols"]
+        total = per * world
+    if args.config == 5:
+        par = f"partitioned1d{world}" if world > 1 else "single"
+    elif args.config == 2 and args.partitioned and world > 1:
+        par = f"partitioned1d{world}"
+    else:
+        par = f"replicas{world}" if world > 1 else "single"
+    return {"workload": cfg["workload"], "config_index": args.config,
+            "elements_total": total, "elements_per_gpu": per,
+            "l2": "64 rotating 4 MiB inputs (256 MiB > L2)" if args.config == 1 else "inputs larger than L2",
+            "parallelism": par}
 
 
 # --------------------------------------------------------------------- b200 arm
@@ -600,7 +676,9 @@ def main():
         kernel_step = lambda: H.CudaScanOps().scan_axis_into(  # noqa: E731
             CumSumOp, dev, StridedView(x, lay), 0, 0, StridedView(y, lay), stream=sp)
         units = n
+        slice_lo = rank * ((total + world - 1) // world)
     dev.synchronize_stream(sp)
+    total_units = units * world
 
     # ---------------- warm-up, then exactly K timed steps -------------
     with torch.cuda.stream(stream):
@@ -628,6 +706,11 @@ def main():
     per_launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     ms_per_step = total_ms / args.steps
     value = bytes_per_step * world * args.steps / (total_ms / 1e3) / 1e9
+
+    # ---------------- correctness of the timed results (config 5) -------------
+    check_result = None
+    if args.config == 5 and not args.no_check:
+        check_result = check_config5(dev, x, y, s64, n, slice_lo, cfg["n"], rank, world, dist, local)
 
     # ---------------- dominant kernel roofline -------------
     if kernel_step is not None:
@@ -698,14 +781,9 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6),
             "higher_is_better": True, "scaling": "weak" if args.config != 5 else "strong",
             "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
-            "config": {"workload": cfg["workload"], "config_index": args.config,
-                       "elements_per_gpu": units,
-                       "elements_per_s": round(units * world / (ms_per_step / 1e3), 1),
-                       "fraction_of_hbm_peak": round(value / world / peak, 4),
-                       "l2": "inputs larger than L2" if args.config != 1 else
-                             "64 rotating 4 MiB inputs (256 MiB > L2)",
-                       "parallelism": f"partitioned1d{world}" if comm else
-                                      (f"replicas{world}" if world > 1 else "single")},
+            "config": config_dict(args, cfg, world),
+            "elements_per_s": round(total_units / (ms_per_step / 1e3), 1),
+            "fraction_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": cfg["kernel"], "peak_source": peak_kind,
@@ -716,13 +794,69 @@ def main():
             **({"latency_mode": latency} if latency else {}),
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * args.steps,
+            **({"check": check_result["status"], "check_detail": check_result["detail"]} if check_result else {}),
         }
         print(json.dumps(line), flush=True)
     if comm:
         comm.destroy()
     if dist:
         dist.destroy_process_group()
-    return 0
+    return 0 if check_result is None or check_result["status"] == "ok" else 1
+
+
+def check_config5(dev, x, y, s64, n, lo, total, rank, world, dist, local):
+    """Element-by-element check of the timed step's results with numpy (not
+    the oracle: the product's own bench checks itself independently).  Each
+    rank downloads its slice in 1 GiB pieces and checks y = carry + the
+    wrapping running sum of x, where carry is read off y[0] - x[0]; the ranks
+    then exchange their slice sums and carries: every carry must be the
+    wrapped sum of the lower ranks' slices, and the i64 result on every rank
+    the sum of all slices."""
+    import torch
+
+    def wrap32(v):
+        return (v + (1 << 31)) % (1 << 32) - (1 << 31)
+
+    piece = 1 << 28
+    xs, ys = np.empty(min(piece, n), np.int32), np.empty(min(piece, n), np.int32)
+    local_sum, carry, running, bad = 0, None, 0, -1
+    t0 = time.perf_counter()
+    for off in range(0, n, piece):
+        m = min(piece, n - off)
+        dev.download_sub_buffer(x, off, xs[:m])
+        dev.download_sub_buffer(y, off, ys[:m])
+        if carry is None:
+            carry = wrap32(int(ys[0]) - int(xs[0]))
+            running = carry
+        want = np.cumsum(xs[:m], dtype=np.int32)
+        want += np.int32(running)  # wraps, as the scan does
+        if bad < 0 and not np.array_equal(want, ys[:m]):
+            bad = off + int(np.argmax(want != ys[:m]))
+        running = int(want[-1])
+        local_sum += int(xs[:m].sum(dtype=np.int64))
+    got_sum = int(dev.download_owned(s64)[0])
+    mine = torch.tensor([local_sum, carry, got_sum, bad], dtype=torch.int64, device=f"cuda:{local}")
+    if dist:
+        every = torch.empty(world * 4, dtype=torch.int64, device=f"cuda:{local}")
+        dist.all_gather_into_tensor(every, mine)
+        rows = every.view(world, 4).cpu().tolist()
+    else:
+        rows = [mine.cpu().tolist()]
+    grand = sum(r[0] for r in rows)
+    problems = []
+    for r, (ls, c, gs, b) in enumerate(rows):
+        if b >= 0:
+            problems.append(f"rank {r}: scan differs from element {b} of its slice")
+        if c != wrap32(sum(q[0] for q in rows[:r])):
+            problems.append(f"rank {r}: carry {c} is not the wrapped sum of the lower slices")
+        if gs != grand:
+            problems.append(f"rank {r}: i64 sum {gs} != {grand}")
+    detail = (f"{total} elements on {world} rank(s): every scan output against a numpy wrapping cumsum of the "
+              f"downloaded input seeded with the rank's carry, carries against the lower slices' sums, the "
+              f"i64 sum ({grand}) against numpy; {time.perf_counter() - t0:.1f} s")
+    if problems:
+        return {"status": "failed", "detail": "; ".join(problems[:4])}
+    return {"status": "ok", "detail": detail}
 
 
 def run_e2e(args, cfg, dev, stream, sp, world, rank, comm, max_over_ranks, barrier):
@@ -736,42 +870,57 @@ def run_e2e(args, cfg, dev, stream, sp, world, rank, comm, max_over_ranks, barri
     from hephaestus_b200 import _native as N
     from hephaestus_b200.core import CumSumOp, Layout, StridedView, SumOp, check
 
+    pins = []
+
     def pinned(nbytes):
         p = ctypes.c_void_p()
         check(N.lib.heph_host_alloc_pinned(nbytes, ctypes.byref(p)))
+        pins.append(p)
         return p
 
-    if args.config in (2, 5):
-        dt = np.uint32 if args.config == 2 else np.int32
-        total = cfg["n"]
-        n = total if args.config == 2 else min((total + world - 1) // world, total - rank * ((total + world - 1) // world))
-        es = 4
-        hin, hout = pinned(n * es), pinned(n * es)
-        x = dev.alloc_uninitialized(dt, n)
-        y = dev.alloc_uninitialized(dt, n)
+    if args.config == 2:
+        n = cfg["n"]
+        hin, hout = pinned(4 * n), pinned(4 * n)
+        x = dev.alloc_uninitialized(np.uint32, n)
+        y = dev.alloc_uninitialized(np.uint32, n)
         lay = Layout.c_contiguous([n])
-        ops = H.CudaScanOps()
-
-        def e2e_step_serial():
-            check(N.lib.heph_buffer_upload_async(dev.handle, x.handle, 0, hin, n, ctypes.c_void_p(sp)))
-            if comm:
-                comm.scan_into(CumSumOp, StridedView(x, lay), StridedView(y, lay), exclusive=args.config == 2,
-                               stream=sp)
-            else:
-                ops.scan_axis_into(CumSumOp, dev, StridedView(x, lay), 0, 0, StridedView(y, lay),
-                                   exclusive=args.config == 2, stream=sp)
-            check(N.lib.heph_buffer_download_async(dev.handle, y.handle, 0, hout, n, ctypes.c_void_p(sp)))
 
         if comm is None:
             # One call through the public host-buffer entry point: chunked
             # copies and scans overlapped on both copy engines.
             def e2e_step():
-                check(N.lib.heph_scan_host(dev.handle, N.SUM, int(args.config == 2),
-                                           N.U32 if args.config == 2 else N.I32, hin, hout, n, 0))
+                check(N.lib.heph_scan_host(dev.handle, N.SUM, 1, N.U32, hin, hout, n, 0))
         else:
-            e2e_step = e2e_step_serial
-        bytes_step = 8 * n
-        h2d, d2h = n * es, n * es
+            def e2e_step():
+                check(N.lib.heph_buffer_upload_async(dev.handle, x.handle, 0, hin, n, ctypes.c_void_p(sp)))
+                comm.scan_into(CumSumOp, StridedView(x, lay), StridedView(y, lay), exclusive=True, stream=sp)
+                check(N.lib.heph_buffer_download_async(dev.handle, y.handle, 0, hout, n, ctypes.c_void_p(sp)))
+        bytes_step, h2d, d2h = 8 * n, 4 * n, 4 * n
+    elif args.config == 5:
+        total = cfg["n"]
+        per = (total + world - 1) // world
+        n = min(per, total - rank * per)
+        hin, hout, hsum = pinned(4 * n), pinned(4 * n), pinned(8)
+        x = dev.alloc_uninitialized(np.int32, n)
+        y = dev.alloc_uninitialized(np.int32, n)
+        s64 = dev.alloc_zeroed(np.int64, 1)
+        lay, one = Layout.c_contiguous([n]), Layout.c_contiguous([1])
+        if comm is None:
+            # One call through the public host-buffer entry point: the slice
+            # flows through device slots in chunks, uploads, scans + sums and
+            # downloads overlapped on both copy engines.
+            def e2e_step():
+                check(N.lib.heph_scan_reduce_host(dev.handle, N.SUM, 0, N.I32, hin, hout, n, N.SUM, N.I64, hsum, 0))
+        else:
+            # The carry needs every rank's total first, so the slice is
+            # uploaded whole, then scanned + summed, then downloaded.
+            def e2e_step():
+                check(N.lib.heph_buffer_upload_async(dev.handle, x.handle, 0, hin, n, ctypes.c_void_p(sp)))
+                comm.scan_reduce_into(CumSumOp, StridedView(x, lay), StridedView(y, lay), SumOp,
+                                      StridedView(s64, one), stream=sp)
+                check(N.lib.heph_buffer_download_async(dev.handle, y.handle, 0, hout, n, ctypes.c_void_p(sp)))
+                check(N.lib.heph_buffer_download_async(dev.handle, s64.handle, 0, hsum, 1, ctypes.c_void_p(sp)))
+        bytes_step, h2d, d2h = 12 * n, 4 * n, 4 * n + 8
     elif args.config == 1:
         n = cfg["n"]
         hin = pinned(4 * n)
@@ -857,6 +1006,8 @@ def run_e2e(args, cfg, dev, stream, sp, world, rank, comm, max_over_ranks, barri
         e2e_step()
         dev.synchronize_stream(sp)
     ms = max_over_ranks((time.perf_counter() - t0) * 1e3) / steps
+    for p in pins:  # the host memory goes back before the CPU baseline runs
+        check(N.lib.heph_host_free_pinned(p))
     return {"value": round(bytes_step * world / (ms / 1e3) / 1e9, 3), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4),
             "steps": steps}

@@ -112,6 +112,7 @@ SIGNATURES = [
     ("heph_partitioned_scan_reduce", _st, [_vp, _i, _i, _vp, _lp, _vp, _lp, _i, _vp, _lp, _vp]),
     ("heph_scan_seeded", _st, [_vp, _i, _i, _vp, _lp, _vp, _lp, _vp, _u64, _vp]),
     ("heph_scan_host", _st, [_vp, _i, _i, _i, _vp, _vp, _u64, _u64]),
+    ("heph_scan_reduce_host", _st, [_vp, _i, _i, _i, _vp, _vp, _u64, _i, _i, _vp, _u64]),
     ("heph_reduce_full_noalloc", _st, [_i, _i, _i, _vp, _u64, _vp, _vp]),
     ("heph_synth_fill", _st, [_vp, _vp, _u64, _u64, _i, _u64, _u64, _vp]),
     ("heph_synth_inject_row_ties", _st, [_vp, _vp, _u64, _u64, _u64, _vp]),

@@ -154,6 +154,26 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
+// Deadline of a wait on another CTA's (or another launch's) progress, kept by
+// the global timer rather than by a poll count: __nanosleep is only a hint,
+// and on a time-sliced GPU a slow but live partner must not be mistaken for
+// a lost one.  The timer is read every 64 polls; the clock starts at the
+// first read, so a wait that succeeds within 63 polls never reads it.
+constexpr uint64_t kWaitDeadlineNs = 2000000000ull;  // 2 s
+struct WaitDeadline {
+    uint64_t start = 0;
+    uint32_t polls = 0;
+    __device__ __forceinline__ bool expired() {
+        if ((++polls & 63u) != 0) return false;
+        const uint64_t now = globaltimer_ns();
+        if (start == 0) {
+            start = now;
+            return false;
+        }
+        return now - start > kWaitDeadlineNs;
+    }
+};
+
 // Sets a device-side error bit visible to the host after synchronisation.
 __device__ __forceinline__ void raise_device_error(unsigned int *err, unsigned int code) {
     if (err) atomicOr(err, code);

@@ -9,6 +9,7 @@
 // chunk k-1, kept on the device by a one-thread kernel, so the result equals
 // the whole-buffer scan and no host synchronisation happens between chunks.
 #include <algorithm>
+#include <cstring>
 #include <utility>
 #include <vector>
 
@@ -24,6 +25,31 @@ template <typename T, int OP>
 __global__ void carry_after_chunk(const T *last_out, const T *last_in, int exclusive, T *carry) {
     *carry = exclusive ? combine<T, OP>(*last_out, *last_in) : *last_out;
 }
+
+// acc = part (first chunk) or combine(acc, part): the running reduction of
+// the chunks so far, folded in chunk order.
+template <typename Tacc>
+__global__ void fold_chunk_partial(Tacc *acc, const Tacc *part, int op, int first) {
+    Tacc v = *part;
+    if (!first) {
+        const Tacc a = *acc;
+        switch (op) {
+            case OP_SUM: v = combine<Tacc, OP_SUM>(a, v); break;
+            case OP_PROD: v = combine<Tacc, OP_PROD>(a, v); break;
+            case OP_MIN: v = combine<Tacc, OP_MIN>(a, v); break;
+            default: v = combine<Tacc, OP_MAX>(a, v); break;
+        }
+    }
+    *acc = v;
+}
+
+// Optional full reduction of the same host input, computed chunk by chunk
+// while the scan pipeline runs.
+struct HostReduce {
+    int op = -1;  // -1: none
+    heph_dtype acc = HEPH_F32;
+    void *host_out = nullptr;
+};
 
 constexpr int kSlots = 3;
 
@@ -72,7 +98,8 @@ struct PipelineStreams {
 };
 
 template <typename T, int OP>
-heph_status scan_host_typed(Device *dev, int exclusive, const T *host_in, T *host_out, uint64_t n, uint64_t chunk) {
+heph_status scan_host_typed(Device *dev, int exclusive, const T *host_in, T *host_out, uint64_t n, uint64_t chunk,
+                            const HostReduce &red) {
     cudaStream_t cs = dev->stream;
     PipelineStreams ps;
     HEPH_CUDA_TRY(cudaStreamCreateWithFlags(&ps.h2d, cudaStreamNonBlocking), HEPH_DISPATCH_FAILED, "stream");
@@ -82,12 +109,17 @@ heph_status scan_host_typed(Device *dev, int exclusive, const T *host_in, T *hos
         HEPH_CUDA_TRY(cudaEventCreateWithFlags(&ps.scanned[s], cudaEventDisableTiming), HEPH_DISPATCH_FAILED, "event");
         HEPH_CUDA_TRY(cudaEventCreateWithFlags(&ps.drained[s], cudaEventDisableTiming), HEPH_DISPATCH_FAILED, "event");
     }
-    // Slots: [in chunk][out chunk] per slot, plus one carry element.
+    // Slots: [in chunk][out chunk] per slot, one carry element, then (with a
+    // reduction) the chunk's partial and the running reduction, 8 bytes each.
     const uint64_t slots = std::min<uint64_t>(kSlots, (n + chunk - 1) / chunk);
+    const uint64_t carry_bytes = (2 * slots * chunk + 1) * sizeof(T);
+    const uint64_t red_off = (carry_bytes + 7) / 8 * 8;
     T *mem = nullptr;
-    HEPH_CUDA_TRY(cudaMallocFromPoolAsync((void **)&mem, (2 * slots * chunk + 1) * sizeof(T), dev->pool, cs),
+    HEPH_CUDA_TRY(cudaMallocFromPoolAsync((void **)&mem, red_off + 16, dev->pool, cs),
                   HEPH_ALLOCATION_FAILED, "pipeline staging allocation");
     T *carry = mem + 2 * slots * chunk;
+    void *red_part = reinterpret_cast<char *>(mem) + red_off;
+    void *red_acc = reinterpret_cast<char *>(mem) + red_off + 8;
     // The copy streams must not touch the staging memory before it exists.
     cudaEvent_t ready;
     HEPH_CUDA_TRY(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming), HEPH_DISPATCH_FAILED, "event");
@@ -114,6 +146,20 @@ heph_status scan_host_typed(Device *dev, int exclusive, const T *host_in, T *hos
         p.in_r = p.out_r = 1;
         st = launch_scan(dev, cs, OP, DtypeOf<T>::value, din, dout, p, false, exclusive != 0, k ? carry : nullptr);
         if (st != HEPH_OK) break;
+        if (red.op >= 0) {
+            heph_layout l{};
+            l.rank = 1;
+            l.shape[0] = len;
+            l.strides[0] = 1;
+            st = launch_reduce_full(dev, cs, red.op, DtypeOf<T>::value, red.acc, din, l, len, red_part);
+            if (st != HEPH_OK) break;
+            st = dispatch_dtype(red.acc, [&]<typename A>() -> heph_status {
+                fold_chunk_partial<A><<<1, 1, 0, cs>>>(static_cast<A *>(red_acc), static_cast<const A *>(red_part),
+                                                       red.op, k == 0);
+                return HEPH_OK;
+            });
+            if (st != HEPH_OK) break;
+        }
         carry_after_chunk<T, OP><<<1, 1, 0, cs>>>(dout + len - 1, din + len - 1, exclusive, carry);
         cudaEventRecord(ps.scanned[s], cs);
         cudaStreamWaitEvent(ps.d2h, ps.scanned[s], 0);
@@ -123,6 +169,9 @@ heph_status scan_host_typed(Device *dev, int exclusive, const T *host_in, T *hos
         }
         cudaEventRecord(ps.drained[s], ps.d2h);
     }
+    if (st == HEPH_OK && red.op >= 0 &&
+        cudaMemcpyAsync(red.host_out, red_acc, dtype_size(red.acc), cudaMemcpyDeviceToHost, cs) != cudaSuccess)
+        st = cuda_fail(HEPH_TRANSFER_FAILED, cudaGetLastError(), "device-to-host copy of the reduction");
     cudaError_t e1 = cudaStreamSynchronize(ps.d2h), e2 = cudaStreamSynchronize(ps.h2d);
     cudaFreeAsync(mem, cs);
     cudaError_t e3 = cudaStreamSynchronize(cs);
@@ -137,23 +186,65 @@ heph_status scan_host_typed(Device *dev, int exclusive, const T *host_in, T *hos
 
 using namespace heph;
 
-extern "C" heph_status heph_scan_host(heph_device *device, heph_op op, int exclusive, heph_dtype dtype,
-                                      const void *host_in, void *host_out, uint64_t count, uint64_t chunk_elems) {
+namespace heph {
+namespace {
+
+heph_status scan_host_entry(heph_device *device, heph_op op, int exclusive, heph_dtype dtype, const void *host_in,
+                            void *host_out, uint64_t count, uint64_t chunk_elems, const HostReduce &red) {
     if (!device) return fail(HEPH_INVALID_CONFIGURATION, "null device");
     if (count && (!host_in || !host_out)) return fail(HEPH_INVALID_CONFIGURATION, "null host pointer");
     if (op != HEPH_SUM && op != HEPH_PROD)
         return fail(HEPH_INVALID_CONFIGURATION, "scans support the sum (cumsum) and product (cumprod) operators");
     if (!dtype_valid(dtype)) return fail(HEPH_INVALID_CONFIGURATION, "unknown element type");
     if (host_in == host_out && count) return fail(HEPH_DISPATCH_FAILED, "scan output buffer must not alias input buffer");
-    if (count == 0) return HEPH_OK;
     heph_status st = bind(device);
     if (st != HEPH_OK) return st;
+    if (count == 0) {
+        if (red.op < 0) return HEPH_OK;
+        // The empty reduction is the operator's identity.
+        return dispatch_dtype(red.acc, [&]<typename A>() -> heph_status {
+            A v{};
+            switch (red.op) {
+                case OP_SUM: v = identity<A, OP_SUM>(); break;
+                case OP_PROD: v = identity<A, OP_PROD>(); break;
+                case OP_MIN: v = identity<A, OP_MIN>(); break;
+                default: v = identity<A, OP_MAX>(); break;
+            }
+            std::memcpy(red.host_out, &v, sizeof(A));
+            return HEPH_OK;
+        });
+    }
     const uint64_t chunk = chunk_elems ? chunk_elems : (64ull << 20) / dtype_size(dtype);
     return dispatch_dtype(dtype, [&]<typename T>() -> heph_status {
         if (op == HEPH_SUM)
             return scan_host_typed<T, OP_SUM>(device, exclusive, static_cast<const T *>(host_in),
-                                              static_cast<T *>(host_out), count, chunk);
+                                              static_cast<T *>(host_out), count, chunk, red);
         return scan_host_typed<T, OP_PROD>(device, exclusive, static_cast<const T *>(host_in),
-                                           static_cast<T *>(host_out), count, chunk);
+                                           static_cast<T *>(host_out), count, chunk, red);
     });
+}
+
+}  // namespace
+}  // namespace heph
+
+extern "C" heph_status heph_scan_host(heph_device *device, heph_op op, int exclusive, heph_dtype dtype,
+                                      const void *host_in, void *host_out, uint64_t count, uint64_t chunk_elems) {
+    return scan_host_entry(device, op, exclusive, dtype, host_in, host_out, count, chunk_elems, HostReduce{});
+}
+
+extern "C" heph_status heph_scan_reduce_host(heph_device *device, heph_op scan_op, int exclusive, heph_dtype dtype,
+                                             const void *host_in, void *host_out, uint64_t count, heph_op reduce_op,
+                                             heph_dtype acc_dtype, void *host_reduce_out, uint64_t chunk_elems) {
+    if (!host_reduce_out) return fail(HEPH_INVALID_CONFIGURATION, "null host pointer");
+    if (reduce_op != HEPH_SUM && reduce_op != HEPH_PROD && reduce_op != HEPH_MIN && reduce_op != HEPH_MAX)
+        return fail(HEPH_INVALID_CONFIGURATION, "full reduction supports sum, prod, min and max");
+    const bool widen = (dtype == HEPH_I32 && acc_dtype == HEPH_I64) || (dtype == HEPH_F32 && acc_dtype == HEPH_F64);
+    if (acc_dtype != dtype && !widen)
+        return fail(HEPH_INVALID_CONFIGURATION,
+                    "full reduction output type must match the input type or widen it (i32->i64, f32->f64)");
+    HostReduce red;
+    red.op = (int)reduce_op;
+    red.acc = acc_dtype;
+    red.host_out = host_reduce_out;
+    return scan_host_entry(device, scan_op, exclusive, dtype, host_in, host_out, count, chunk_elems, red);
 }

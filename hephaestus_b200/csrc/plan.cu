@@ -168,9 +168,12 @@ heph_status plan_axis_scan(const heph_layout &in, uint64_t in_len, const heph_la
                            uint64_t out_len, uint32_t axis, bool alias, bool *noop,
                            AxisProblem *p) {
     *noop = false;
+    // The reference accepts rank 2 only (core accelerator/scan.rs:519-523);
+    // rank 1 (one line, the 1-D case) is accepted here as an extension.  Any
+    // other rank is rejected with the reference's wording.
     if (in.rank != 1 && in.rank != 2)
         return fail(HEPH_DISPATCH_FAILED,
-                    "cuda-sm100a scan supports rank 1 or 2, got rank " + std::to_string(in.rank));
+                    "cuda-sm100a scan supports rank 2 only, got rank " + std::to_string(in.rank));
     if (axis >= in.rank)
         return fail(HEPH_DISPATCH_FAILED, "scan axis " + std::to_string(axis) +
                                               " is out of bounds for rank-" +

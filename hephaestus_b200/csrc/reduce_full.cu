@@ -524,22 +524,17 @@ constexpr int kStaticPartials = 2048;  // CTA partials (8 bytes each) the array 
 // [0, 16 KiB): partials of up to kStaticPartials CTAs; then the ticket.
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticPartials * 8 + 256];
 
-// Device address of g_static_scratch, looked up once per device.
-std::mutex g_static_mu;
-void *g_static_addr[256] = {};
-
+// Device address of g_static_scratch in the CURRENT context.  A symbol's
+// address belongs to a context's load of this module, not to a device
+// ordinal (a driver-API embedder may run on a non-primary context, and
+// cudaDeviceReset unloads the module), so it is looked up on every call; the
+// lookup allocates nothing.  The first call in a context loads the module
+// there, so that first call should come before any stream capture.
 heph_status static_scratch_address(void **out) {
-    int dev = 0;
-    HEPH_CUDA_TRY(cudaGetDevice(&dev), HEPH_DEVICE_UNAVAILABLE, "cudaGetDevice");
-    if (dev < 0 || dev >= 256) return fail(HEPH_DEVICE_UNAVAILABLE, "device ordinal out of range");
-    std::lock_guard<std::mutex> lock(g_static_mu);
-    if (!g_static_addr[dev]) {
-        void *p = nullptr;
-        HEPH_CUDA_TRY(cudaGetSymbolAddress(&p, g_static_scratch), HEPH_DEVICE_UNAVAILABLE,
-                      "static scratch address lookup");
-        g_static_addr[dev] = p;
-    }
-    *out = g_static_addr[dev];
+    void *p = nullptr;
+    HEPH_CUDA_TRY(cudaGetSymbolAddress(&p, g_static_scratch), HEPH_DEVICE_UNAVAILABLE,
+                  "static scratch address lookup");
+    *out = p;
     return HEPH_OK;
 }
 

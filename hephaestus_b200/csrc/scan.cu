@@ -38,7 +38,6 @@ namespace heph {
 
 constexpr int kScanThreads = 256;
 constexpr int kScanWarps = kScanThreads / 32;
-constexpr uint32_t kPolls = 1u << 20;        // bounded waits on other CTAs
 constexpr int kLookbackVectors = 8;          // look-back tile: 8 x 128-bit per thread (32 KiB)
 constexpr int kLookbackVectorsSmall = 4;     // look-back tile for lines under 32 KiB (16 KiB)
 constexpr uint64_t kInterleaveMinTiles = 2;  // look-back tiles per line from which lines interleave
@@ -393,7 +392,7 @@ template <typename T, int OP>
 __device__ T lookback(const LookbackParams<T> &p, uint64_t tile, uint64_t pos, int lane) {
     T excl = identity<T, OP>();
     int64_t back = 1;  // distance of this round's first predecessor
-    uint32_t polls = 0;
+    WaitDeadline deadline;  // every lane keeps the same count; lane 0 decides
     while (true) {
         const int64_t d = back + lane;
         const bool in_range = d <= (int64_t)pos;
@@ -402,7 +401,7 @@ __device__ T lookback(const LookbackParams<T> &p, uint64_t tile, uint64_t pos, i
         const uint64_t idx = tile - (uint64_t)d * p.pos_step;
         if (in_range) state = read_status(p.status, idx, val);
         while (__any_sync(kFullMask, state == kStateInvalid)) {
-            if (++polls > kPolls) {
+            if (__shfl_sync(kFullMask, (int)deadline.expired(), 0)) {
                 if (lane == 0) raise_device_error(p.err, DEVERR_LOOKBACK_TIMEOUT);
                 return excl;
             }
@@ -576,24 +575,18 @@ __device__ __forceinline__ void bulk_load(void *dst_smem, const void *src, uint3
                  : "memory");
 }
 
-// Waits for phase `parity` of `bar`.  Bounded in time (kMbarWaitNs by the
-// global timer, checked every 64 polls): past it the device error bit is
-// raised and the wait gives up.
-constexpr uint64_t kMbarWaitNs = 2000000000ull;
+// Waits for phase `parity` of `bar`.  Bounded in time (WaitDeadline): past
+// the deadline the device error bit is raised and the wait gives up.
 __device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, unsigned int *err) {
-    uint64_t start = 0;
-    for (uint32_t polls = 1;; ++polls) {
+    WaitDeadline deadline;
+    while (true) {
         uint32_t done;
         asm volatile("{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n selp.u32 %0, 1, 0, P;\n}"
                      : "=r"(done)
                      : "r"(smem_addr(bar)), "r"(parity)
                      : "memory");
         if (done) return;
-        if ((polls & 63u) == 0) {
-            const uint64_t now = globaltimer_ns();
-            if (start == 0) start = now;
-            else if (now - start > kMbarWaitNs) break;
-        }
+        if (deadline.expired()) break;
     }
     if (threadIdx.x == 0) raise_device_error(err, DEVERR_BULK_TIMEOUT);
 }
@@ -740,9 +733,9 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
             } else {
                 ok = read_status(p.status, c * G + q, v) != kStateInvalid;
             }
-            uint32_t polls = 0;
+            WaitDeadline deadline;
             while (!ok) {
-                if (++polls > kPolls) {
+                if (deadline.expired()) {
                     raise_device_error(p.err, DEVERR_LOOKBACK_TIMEOUT);
                     v = identity<T, OP>();
                     break;

@@ -202,6 +202,26 @@ class CudaScanOps:
                                    host_in.ctypes.data_as(ctypes.c_void_p),
                                    host_out.ctypes.data_as(ctypes.c_void_p), host_in.size, int(chunk_elems)))
 
+    def scan_reduce_host(self, op, device, host_in, host_out, reduce_op, acc_dtype=None, exclusive: bool = False,
+                         chunk_elems: int = 0):
+        """[EXT] scan_host plus the full reduction `reduce_op` of the same host
+        array (heph_scan_reduce_host), accumulated in `acc_dtype` (the input
+        type, or i64 for i32 / f64 for f32).  Returns the reduction."""
+        import numpy as np
+
+        from .core import InvalidConfiguration, dtype_code
+        if host_in.dtype != host_out.dtype or host_in.size != host_out.size:
+            raise InvalidConfiguration("host input and output must have the same type and length")
+        if not (host_in.flags.c_contiguous and host_out.flags.c_contiguous):
+            raise InvalidConfiguration("host arrays must be C-contiguous")
+        acc = np.zeros(1, dtype=host_in.dtype if acc_dtype is None else acc_dtype)
+        check(N.lib.heph_scan_reduce_host(device.handle, op.code, int(bool(exclusive)), dtype_code(host_in.dtype),
+                                          host_in.ctypes.data_as(ctypes.c_void_p),
+                                          host_out.ctypes.data_as(ctypes.c_void_p), host_in.size, reduce_op.code,
+                                          dtype_code(acc.dtype), acc.ctypes.data_as(ctypes.c_void_p),
+                                          int(chunk_elems)))
+        return acc[0]
+
     def dispatch_scan(self, device, prepared: Prepared, stream=None):
         _dispatch(device, prepared, stream)
 

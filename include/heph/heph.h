@@ -6,8 +6,8 @@
  * `ComputeDevice`, `FullReductionOps`, `AxisReductionOps` and `ScanOps`
  * together with the `HephaestusError` vocabulary.  Every entry point below
  * names the reference interface it replaces as `path:line` within that
- * project.  A Rust backend crate binds these symbols 1:1 (the bindings are
- * shown in INTEGRATION.md at the repository root).
+ * project.  A Rust backend crate binds these symbols 1:1 through an
+ * `extern "C"` block of the same names and argument types.
  *
  * Conventions
  *  - Every fallible call returns a heph_status.  On failure a thread-local
@@ -213,7 +213,10 @@ heph_status heph_plan_axis_reduction(const heph_layout *input, uint64_t input_le
                                      const heph_layout *output, uint64_t output_len,
                                      uint32_t axis, int buffers_alias, int *out_noop);
 /* Validation half of plan_axis_scan — core scan.rs:87-178 — with 64-bit
- * extents, rank 1 or 2 [EXT: rank 1].  Sets *out_noop = 1 when empty. */
+ * extents.  Rank 2 as in the reference; [EXT] rank 1 (a single line) is also
+ * accepted; every other rank is rejected with the reference's message
+ * "cuda-sm100a scan supports rank 2 only, got rank N"
+ * (core accelerator/scan.rs:519-523).  Sets *out_noop = 1 when empty. */
 heph_status heph_plan_axis_scan(const heph_layout *input, uint64_t input_len,
                                 const heph_layout *output, uint64_t output_len,
                                 uint32_t axis, int buffers_alias, int *out_noop);
@@ -421,6 +424,18 @@ heph_status heph_scan_seeded(heph_device *device, heph_op op, int exclusive,
 heph_status heph_scan_host(heph_device *device, heph_op op, int exclusive, heph_dtype dtype,
                            const void *host_in, void *host_out, uint64_t count, uint64_t chunk_elems);
 
+/* [EXT] heph_scan_host plus a full reduction of the same host input (the
+ * scan + sum pair of the partitioned 1-D case on one device): every chunk is
+ * also reduced on the device while it is staged, the chunks' results folded
+ * in order, and the single result (acc_dtype: the input type or its widening
+ * I32->I64 / F32->F64; op SUM/PROD/MIN/MAX; the identity when count == 0)
+ * written to *host_reduce_out.  Replaces upload + ScanOps::scan_axis_into +
+ * FullReductionOps::reduce_full_into + download (core scan.rs:219,
+ * reduction.rs:243, device.rs:135,147) for host data. */
+heph_status heph_scan_reduce_host(heph_device *device, heph_op scan_op, int exclusive, heph_dtype dtype,
+                                  const void *host_in, void *host_out, uint64_t count, heph_op reduce_op,
+                                  heph_dtype acc_dtype, void *host_reduce_out, uint64_t chunk_elems);
+
 /* ------------------------------------------ allocation-free full reduction */
 
 /* No counterpart in the reference: an extra entry point for callers that
@@ -439,9 +454,11 @@ heph_status heph_scan_host(heph_device *device, heph_op op, int exclusive, heph_
  * Scratch: a static 16 KiB + 256 B device array inside the library (every GPU
  * that loads the library keeps it until the process exits) that holds one
  * partial per CTA for at most 2048 CTAs; a launch that would need more is
- * rejected with HEPH_INVALID_CONFIGURATION.  The first call on each device
- * looks up that array's device address (no allocation); make that first call
- * before any stream capture.  All calls share the one array, so calls whose
+ * rejected with HEPH_INVALID_CONFIGURATION.  Every call looks up that
+ * array's device address in the calling thread's current context (no
+ * allocation), so non-primary driver-API contexts are served too; the first
+ * call in a context loads the library's kernels there, so make that first
+ * call before any stream capture.  All calls share the one array, so calls whose
  * kernels overlap on the GPU (different streams, or several host threads)
  * race and must be serialised by the caller. */
 heph_status heph_reduce_full_noalloc(heph_op op, heph_dtype in_dtype, heph_dtype out_dtype,

@@ -1,7 +1,15 @@
 """Worker of tests/test_multigpu_gpu.py, launched with torch.distributed.run:
 every rank owns one contiguous slice of a global buffer generated on its GPU,
 runs the partitioned scan / reduce through hephaestus_b200.dist, and writes its
-slice of the results to the directory in argv[1]."""
+slice of the results to the directory in argv[1].
+
+With argv[2] == "large" the buffer is 2^28 + 5 i32 elements, and every rank
+checks its own slice in process instead: it downloads its input, the ranks
+exchange the oracle's totals of their slices over gloo, and the oracle scans
+the slice seeded with the lower ranks' carry; the fused and the separate
+calls must both match it bit for bit, and the i64 sum must equal the oracle's
+widening sum of the whole buffer.  Each rank writes ok_<rank>.txt when its
+slice matches."""
 import os
 import sys
 
@@ -17,6 +25,38 @@ from hephaestus_b200.core import CumSumOp, Layout, MaxOp, StridedView, SumOp  # 
 from hephaestus_b200.dist import Communicator  # noqa: E402
 
 TOTAL = 25_000_003
+LARGE_TOTAL = (1 << 28) + 5
+
+
+def check_large(out_dir, dev, comm, rank, world):
+    from oracle import host_ref as oracle
+    oracle.build()
+    per = (LARGE_TOTAL + world - 1) // world
+    lo, hi = rank * per, min(LARGE_TOTAL, (rank + 1) * per)
+    n = hi - lo
+    lay, one = Layout.c_contiguous([n]), Layout.c_contiguous([1])
+    x = dev.alloc_uninitialized(np.int32, n)
+    S.synth_fill(dev, x, S.SYNTH_I32_PM1000, seed=4, index_base=lo)
+    yf, ys = dev.alloc_zeroed(np.int32, n), dev.alloc_zeroed(np.int32, n)
+    sf, ss = dev.alloc_zeroed(np.int64, 1), dev.alloc_zeroed(np.int64, 1)
+    for _ in range(2):
+        comm.scan_reduce_into(CumSumOp, StridedView(x, lay), StridedView(yf, lay), SumOp, StridedView(sf, one))
+        comm.scan_into(CumSumOp, StridedView(x, lay), StridedView(ys, lay))
+        comm.reduce_full_into(SumOp, StridedView(x, lay), StridedView(ss, one))
+    hx = dev.download_owned(x)
+    np.testing.assert_array_equal(hx, oracle.generate(oracle.GEN_I32_PM1000, 4, n, index_base=lo))
+    sums = [None] * world
+    dist.all_gather_object(sums, oracle.sum_i32_to_i64_mt(hx))
+    carry = sum(sums[:rank])
+    carry = (carry + (1 << 31)) % (1 << 32) - (1 << 31)
+    want = np.empty_like(hx)
+    oracle.inclusive_scan_i32_mt(hx, want, carry)
+    np.testing.assert_array_equal(dev.download_owned(yf), want)
+    np.testing.assert_array_equal(dev.download_owned(ys), want)
+    assert int(dev.download_owned(sf)[0]) == sum(sums)
+    assert int(dev.download_owned(ss)[0]) == sum(sums)
+    with open(os.path.join(out_dir, f"ok_{rank}.txt"), "w") as fh:
+        fh.write(f"{n} elements from {lo}\n")
 
 
 def main():
@@ -25,6 +65,13 @@ def main():
     rank, world = dist.get_rank(), dist.get_world_size()
     dev = H.CudaDevice(int(os.environ["LOCAL_RANK"]))
     comm = Communicator.from_torch(dev)
+    if len(sys.argv) > 2 and sys.argv[2] == "large":
+        check_large(out_dir, dev, comm, rank, world)
+        dev.synchronize()
+        dist.barrier()
+        comm.destroy()
+        dist.destroy_process_group()
+        return
     per = (TOTAL + world - 1) // world
     lo, hi = rank * per, min(TOTAL, (rank + 1) * per)
     n = hi - lo

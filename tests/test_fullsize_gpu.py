@@ -3,12 +3,10 @@
 Configs 2-4 fit the multithreaded oracle: the device-generated inputs are
 downloaded and the oracle runs on exactly those, element by element
 (integers and argmax indices bit-exact, f64 within 1e-12 * sum|x| per
-column).  Config 5 (2^32 elements, 16 GiB in + 16 GiB out) is checked
-through size-independent properties: the i64 total against the oracle's
-widening sum of the downloaded input, the scan's last element against that
-total, local consistency y[k] = y[k-1] + x[k] in random windows, and at random
-cut points s the scan value y[s-1] against the reduction kernel's total of
-the prefix view [0, s)."""
+column).  Config 5 (2^32 elements, 16 GiB in + 16 GiB out) is compared
+element by element too, in 1 GiB pieces: the oracle scans each downloaded
+piece seeded with its own running carry, and the i64 total is checked against
+the oracle's widening sum."""
 import numpy as np
 import pytest
 
@@ -77,41 +75,26 @@ def test_config5_i32_scan_and_widening_sum_2p32(device, oracle):
     s64 = device.alloc_zeroed(np.int64, 1)
     lay, one = Layout.c_contiguous([n]), Layout.c_contiguous([1])
     H.CudaScanOps().scan_axis_into(CumSumOp, device, StridedView(x, lay), 0, 0, StridedView(y, lay))
-    fops = H.CudaFullReductionOps()
-    fops.reduce_full_into(SumOp, device, StridedView(x, lay), StridedView(s64, one))
+    H.CudaFullReductionOps().reduce_full_into(SumOp, device, StridedView(x, lay), StridedView(s64, one))
     total = int(device.download_owned(s64)[0])
 
-    # The i64 total against the oracle's widening sum of the input, 1 GiB at a time.
+    # Every one of the 2^32 outputs against the oracle's scan of the downloaded
+    # input, 1 GiB at a time, each piece seeded with the oracle's running
+    # (wrapping) carry; the i64 total against the oracle's widening sum.
     chunk = 1 << 28
-    buf = np.empty(chunk, np.int32)
-    want_total = 0
+    xs, ys, want = (np.empty(chunk, np.int32) for _ in range(3))
+    carry, want_total = 0, 0
     for off in range(0, n, chunk):
-        device.download_sub_buffer(x, off, buf)
-        want_total += oracle.sum_i32_to_i64_mt(buf)
+        device.download_sub_buffer(x, off, xs)
+        device.download_sub_buffer(y, off, ys)
+        if off == 0:
+            np.testing.assert_array_equal(xs[:1 << 20], oracle.generate(oracle.GEN_I32_PM1000, 4, 1 << 20))
+        oracle.inclusive_scan_i32_mt(xs, want, carry)
+        np.testing.assert_array_equal(ys, want, err_msg=f"scan piece at {off}")
+        carry = int(want[-1])
+        want_total += oracle.sum_i32_to_i64_mt(xs)
     assert total == want_total
-
-    def wrap32(v):
-        return (v + (1 << 31)) % (1 << 32) - (1 << 31)
-
-    tail = np.empty(1, np.int32)
-    device.download_sub_buffer(y, n - 1, tail)
-    assert int(tail[0]) == wrap32(total)
-
-    rng = np.random.default_rng(5)
-    win = 1 << 16
-    xs, ys = np.empty(win, np.int32), np.empty(win, np.int32)
-    prefix = device.alloc_zeroed(np.int64, 1)
-    for s in [1, (1 << 31) + 3, n - win] + [int(v) for v in rng.integers(1, n - win, size=5)]:
-        # y[s-1] is the wrapped sum of the prefix view [0, s), computed by the
-        # reduction kernel.
-        fops.reduce_full_into(SumOp, device, StridedView(x, Layout.c_contiguous([s])), StridedView(prefix, one))
-        device.download_sub_buffer(y, s - 1, tail)
-        assert int(tail[0]) == wrap32(int(device.download_owned(prefix)[0])), s
-        # Local consistency in the window [s, s + win).
-        device.download_sub_buffer(x, s, xs)
-        device.download_sub_buffer(y, s, ys)
-        want = (int(tail[0]) + np.cumsum(xs.astype(np.int64)))
-        np.testing.assert_array_equal(ys.astype(np.int64), wrap32(want), err_msg=f"window at {s}")
+    assert carry == (total + (1 << 31)) % (1 << 32) - (1 << 31)
 
 
 def test_config1_f32_sum_2p20_batch_and_single(device, oracle):

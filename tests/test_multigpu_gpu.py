@@ -38,3 +38,21 @@ def test_partitioned_scan_and_reduce(tmp_path, oracle):
         assert np.load(tmp_path / f"max_{r}.npy")[0] == xu.max()
         assert np.load(tmp_path / f"fsum_{r}.npy")[0] == int(xi.astype(np.int64).sum())
         assert np.load(tmp_path / f"fmax_{r}.npy")[0] == xu.max()
+
+
+def test_partitioned_scan_and_reduce_large(tmp_path):
+    """2^28 + 5 elements over the ranks (every slice takes the chunked scan),
+    each rank's slice compared in process with the oracle (see dist_worker)."""
+    import torch
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    world = min(world, 8)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", "--master-port", "29534",
+           os.path.join(ROOT, "tests", "dist_worker.py"), str(tmp_path), "large"]
+    res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=900)
+    assert res.returncode == 0, res.stderr[-3000:]
+    for r in range(world):
+        assert (tmp_path / f"ok_{r}.txt").exists(), r

@@ -404,6 +404,34 @@ def test_scan_host_pipeline(device, oracle, dt, exc):
             np.testing.assert_array_equal(y, want, err_msg=f"n={n} chunk={chunk}")
 
 
+@pytest.mark.parametrize("dt,acc,rop", [(np.int32, np.int64, "sum"), (np.uint32, np.uint32, "max"),
+                                        (np.float32, np.float64, "sum"), (np.int64, np.int64, "min")])
+def test_scan_reduce_host_pipeline(device, oracle, dt, acc, rop):
+    """heph_scan_reduce_host: the host-buffer scan plus a full reduction of the
+    same input, chunk by chunk (ragged chunks, the ramp pieces, one chunk)."""
+    from hephaestus_b200.core import MaxOp, MinOp
+    op = {"sum": SumOp, "max": MaxOp, "min": MinOp}[rop]
+    rng = np.random.default_rng(32)
+    ops = CudaScanOps()
+    for n, chunk in [(0, 0), (1, 0), (1000, 7), (100_003, 4096), (5_000_000, 1 << 20), (3_000_001, 0)]:
+        x = rand(dt, n, rng)
+        y = np.empty_like(x)
+        got = ops.scan_reduce_host(CumSumOp, device, x, y, op, acc_dtype=acc, chunk_elems=chunk)
+        want_y = oracle.scan_axis(x, [n], 0) if n else y
+        want = oracle.reduce_full(x, [n], op=op.code, out_dtype=acc) if n else None
+        if np.dtype(dt).kind == "f":
+            np.testing.assert_allclose(y.astype(np.float64), want_y.astype(np.float64), rtol=0, atol=tol(dt, x))
+            if n:
+                assert abs(float(got) - float(want)) <= tol(dt, x), (n, chunk)
+        else:
+            np.testing.assert_array_equal(y, want_y, err_msg=f"n={n} chunk={chunk}")
+            if n:
+                assert got == want, (n, chunk)
+        if n == 0:
+            ident = {"sum": 0, "max": 0, "min": np.iinfo(np.int64).max}[rop]
+            assert got == ident
+
+
 @pytest.mark.parametrize("dt", DTYPES)
 @pytest.mark.parametrize("map_kind", [0, 1, 2, 3, 4])
 def test_map_reduction_parity(device, oracle, dt, map_kind):
@@ -546,6 +574,34 @@ def test_gapped_view_large_and_wide_inner_dim(device):
     i = np.arange(rows, dtype=np.uint64)
     want = (cols * i * ld).sum() + rows * (cols * (cols - 1) // 2)
     assert int(device.download_owned(out)[0]) == int(want) % (1 << 32)
+
+
+@pytest.mark.parametrize("dt,acc,rop", [(np.int32, np.int64, "sum"), (np.uint32, np.uint32, "max"),
+                                        (np.float32, np.float64, "sum"), (np.int64, np.int64, "min")])
+def test_scan_reduce_host_pipeline(device, oracle, dt, acc, rop):
+    """heph_scan_reduce_host: the host-buffer scan plus a full reduction of the
+    same input, chunk by chunk (ragged chunks, the ramp pieces, one chunk)."""
+    from hephaestus_b200.core import MaxOp, MinOp
+    op = {"sum": SumOp, "max": MaxOp, "min": MinOp}[rop]
+    rng = np.random.default_rng(32)
+    ops = CudaScanOps()
+    for n, chunk in [(0, 0), (1, 0), (1000, 7), (100_003, 4096), (5_000_000, 1 << 20), (3_000_001, 0)]:
+        x = rand(dt, n, rng)
+        y = np.empty_like(x)
+        got = ops.scan_reduce_host(CumSumOp, device, x, y, op, acc_dtype=acc, chunk_elems=chunk)
+        want_y = oracle.scan_axis(x, [n], 0) if n else y
+        want = oracle.reduce_full(x, [n], op=op.code, out_dtype=acc) if n else None
+        if np.dtype(dt).kind == "f":
+            np.testing.assert_allclose(y.astype(np.float64), want_y.astype(np.float64), rtol=0, atol=tol(dt, x))
+            if n:
+                assert abs(float(got) - float(want)) <= tol(dt, x), (n, chunk)
+        else:
+            np.testing.assert_array_equal(y, want_y, err_msg=f"n={n} chunk={chunk}")
+            if n:
+                assert got == want, (n, chunk)
+        if n == 0:
+            ident = {"sum": 0, "max": 0, "min": np.iinfo(np.int64).max}[rop]
+            assert got == ident
 
 
 @pytest.mark.parametrize("dt", DTYPES)

@@ -82,7 +82,7 @@ def test_axis_scan_planner_rules():
     st, msg, _ = plan_scan(lay([2, 3], [1, 2], 1), 6, lay([2, 3]), 6, 1)
     assert st == N.DISPATCH_FAILED and msg.startswith("layout rejected:")
     st, msg, _ = plan_scan(lay([2, 2, 2]), 8, lay([2, 2, 2]), 8, 0)
-    assert msg == "cuda-sm100a scan supports rank 1 or 2, got rank 3"
+    assert msg == "cuda-sm100a scan supports rank 2 only, got rank 3"
     st, msg, noop = plan_scan(lay([1 << 32]), 1 << 32, lay([1 << 32]), 1 << 32, 0)
     assert st == N.OK and noop == 0  # 64-bit extents [EXT]
 
