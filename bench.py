@@ -67,6 +67,9 @@ CONFIGS = {
     # many long lines, each a look-back chain of 32 tiles.
     8: dict(workload="u32 inclusive scan along the rows (axis 1) of a [1024 x 262144] row-major matrix, "
                      "h&15 seed 1", rows=1024, cols=262144, dtype="u32", kernel="scan_lookback_kernel"),
+    # A few long lines: all of them in one launch of the chunked kernel.
+    9: dict(workload="u32 inclusive scan along the rows (axis 1) of a [16 x 2^24] row-major matrix, "
+                     "h&15 seed 1", rows=16, cols=1 << 24, dtype="u32", kernel="scan_chunked_kernel"),
 }
 
 
@@ -88,6 +91,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-check", action="store_true",
                     help="config 5: skip the element-by-element check of the results after the timed region")
+    ap.add_argument("--shape", default=None,
+                    help="configs 8/9: ROWSxCOLS instead of the configured matrix (e.g. 64x4194304)")
     ap.add_argument("--n", type=int, default=None,
                     help="override the element count of configs 1, 2 and 5 (small profiling cases)")
     return ap.parse_args()
@@ -224,15 +229,15 @@ def cpu_workload(cfg_id: int, cfg: dict, oracle, threads: int):
         x = data(("x", cfg_id), lambda: oracle.generate(oracle.GEN_F32_UNIFORM_PM1, 0, rows * ld + off))
         return (lambda: oracle.reduce_full(x, [rows, cols], [ld, 1], off)), 4 * rows * cols, \
             f"f32 sum of the [{rows} x {cols}] sub-block (row stride {ld}) (one thread: sequential strided fold)"
-    rows, cols = cfg["rows"], cfg["cols"]  # config 8
-    x = data(("x", 8), lambda: oracle.generate(oracle.GEN_U32_LOW4, 1, rows * cols))
-    out = data(("y", 8), lambda: np.empty_like(x))
+    rows, cols = cfg["rows"], cfg["cols"]  # configs 8 and 9
+    x = data(("x", cfg_id, rows, cols), lambda: oracle.generate(oracle.GEN_U32_LOW4, 1, rows * cols))
+    out = data(("y", cfg_id, rows, cols), lambda: np.empty_like(x))
     return (lambda: oracle.scan_axis(x, [rows, cols], 1, out_storage=out)), 8 * rows * cols, \
         f"u32 row scan of [{rows} x {cols}] (one thread: sequential per-line fold)"
 
 
 def cpu_threads_used(cfg_id: int, threads: int) -> int:
-    return 1 if cfg_id in (6, 7, 8) else threads
+    return 1 if cfg_id in (6, 7, 8, 9) else threads
 
 
 def cpu_sample(cfg_id: int, cfg: dict, oracle, seconds: float = 10.0, threads: int = 0):
@@ -486,6 +491,10 @@ def main():
     elif args.n is not None and args.config in (6, 7):
         cfg["rows"] = int(args.n)
         cfg["workload"] += f" [reduced to {args.n} rows]"
+    if args.shape and args.config in (8, 9):
+        r, c = (int(v) for v in args.shape.lower().split("x"))
+        cfg["rows"], cfg["cols"] = r, c
+        cfg["workload"] = cfg["workload"].split(" of a [")[0] + f" of a [{r} x {c}] row-major matrix, h&15 seed 1"
     if args.impl == "reference":
         return run_reference(args, cfg)
 
@@ -632,7 +641,7 @@ def main():
         kernel_bytes = bytes_per_step
         kernel_step = None
         units = rows * cols
-    elif args.config == 8:
+    elif args.config in (8, 9):
         rows, cols = cfg["rows"], cfg["cols"]
         x = dev.alloc_uninitialized(np.uint32, rows * cols)
         S.synth_fill(dev, x, S.SYNTH_U32_LOW4, seed=1, stream=sp)
@@ -965,7 +974,7 @@ def run_e2e(args, cfg, dev, stream, sp, world, rank, comm, max_over_ranks, barri
                                  stream=sp)
             check(N.lib.heph_buffer_download_async(dev.handle, out.handle, 0, ho, 1, ctypes.c_void_p(sp)))
         bytes_step, h2d, d2h = 4 * rows * cols, 4 * total, 4
-    elif args.config == 8:
+    elif args.config in (8, 9):
         rows, cols = cfg["rows"], cfg["cols"]
         n = rows * cols
         hin, ho = pinned(4 * n), pinned(4 * n)

@@ -19,6 +19,7 @@
 // such a view into a contiguous staging buffer first
 // (full_reduction_seam.rs:96-104).
 #include <algorithm>
+#include <cstdlib>
 
 #include "device_utils.cuh"
 #include "kernels.h"
@@ -287,6 +288,12 @@ static heph_status launch_typed(Device *dev, cudaStream_t stream, const void *ba
     uint64_t want = (count + per_cta - 1) / per_cta;
     const uint64_t cap = (uint64_t)dev->sm_count * (2048 / kReduceThreads);
     unsigned int grid = (unsigned int)std::max<uint64_t>(1, std::min(want, cap));
+    // Experiment knob (read once per process): a fixed grid for dense views.
+    static const int grid_knob = [] {
+        const char *e = getenv("HEPH_REDUCE_GRID");
+        return e ? atoi(e) : 0;
+    }();
+    if (grid_knob > 0) grid = (unsigned int)std::min<uint64_t>((uint64_t)grid_knob, cap);
 
     std::lock_guard<std::mutex> lock(dev->mu);
     Workspace *ws = nullptr;

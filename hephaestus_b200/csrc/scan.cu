@@ -44,7 +44,7 @@ constexpr uint64_t kInterleaveMinTiles = 2;  // look-back tiles per line from wh
 constexpr int kChunkVectors = 4;             // chunked kernel tile: 4 x 128-bit per thread (16 KiB)
 constexpr uint64_t kTwoPassMinTiles = 640;              // single lines of 640+ look-back tiles ...
 constexpr uint64_t kTwoPassMaxBytes = 64ull << 20;      // ... and at most 64 MiB take the two-pass scan
-constexpr uint64_t kPerLineChunkedBytes = 128ull << 20;  // lines of several that take the chunked kernel
+constexpr uint64_t kMultiLineChunkedBytes = 8ull << 20;  // lines of several that take the chunked kernel
 constexpr int kMaxCachedDevices = 64;        // device ordinals with cached launch queries
 constexpr int kChunkMaxBuffers = 6;          // part buffers per CTA of the chunked scan
 constexpr int kChunkMaxPartsPerThread = 2;   // chunked grids have at most 2 x 256 CTAs
@@ -60,6 +60,10 @@ constexpr size_t kStatusBytesPerEntry = 28;
 static int scan_knob(const char *name, int fallback) {
     const char *e = getenv(name);
     return e ? atoi(e) : fallback;
+}
+static uint64_t scan_knob_u64(const char *name, uint64_t fallback) {
+    const char *e = getenv(name);
+    return e ? strtoull(e, nullptr, 10) : fallback;
 }
 
 template <typename T, int JV> struct ScanShape {
@@ -543,15 +547,24 @@ __global__ void __launch_bounds__(kScanThreads) scan_tile_apply_kernel(const T *
 
 // --------------------------------- chunked reduce-then-scan, parts in smem
 
+// The lines of a chunked scan are cut into parts of `part` elements (the last
+// part of a line is ragged when the part does not divide the line).  Part j
+// of line l in scan order has the virtual index v = l * ppl + j; chunk c is
+// the G parts v = c*G .. c*G+G-1, CTA b taking v = c*G + b.  A reverse scan
+// takes the line's parts from its end (physical part ppl-1-j).  One long line
+// is the case lines == 1.
 template <typename T> struct ChunkParams {
     const T *in;
     T *out;
-    uint64_t len;
-    uint64_t part;     // elements per CTA per chunk (a multiple of the tile)
-    uint64_t chunk;    // part * gridDim.x
+    uint64_t len;      // elements per line
+    uint64_t lines;
+    int64_t in_line, out_line;  // element distance between line starts
+    uint64_t ppl;      // parts per line
+    uint64_t parts;    // ppl * lines
+    uint64_t part;     // elements per part (a multiple of the tile)
     uint64_t nchunks;
     StatusView status;
-    const T *carry;
+    const T *carry;    // nullable seed of line 0
     unsigned int *err;
     int reverse, exclusive;
     int buffers;       // shared-memory part buffers per CTA (2..kChunkMaxBuffers)
@@ -591,23 +604,55 @@ __device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, unsign
     if (threadIdx.x == 0) raise_device_error(err, DEVERR_BULK_TIMEOUT);
 }
 
-// Element range [lo, hi) of CTA b's part of logical chunk c.
-template <typename T>
-__device__ __forceinline__ void chunk_part_range(const ChunkParams<T> &p, int b, uint64_t c, uint64_t &lo,
-                                                 uint64_t &hi) {
-    const uint64_t pc = p.reverse ? p.nchunks - 1 - c : c;
-    lo = min(p.len, pc * p.chunk + (uint64_t)b * p.part);
-    hi = min(p.len, lo + p.part);
+// CTA b's part of logical chunk c: element range [lo, hi) within its line
+// (empty past the last line), the line's element offsets, and for the
+// exchange of the chunk's part totals: the index (relative to the chunk's
+// first part) of the first part of this CTA's line (`my_first`) and of the
+// chunk's last line (`last_first`), negative when that line began in an
+// earlier chunk (line 0 counts as begun earlier: the kernel's running carry
+// is its seed).  Thread 0 computes it when it stages the part and keeps it in
+// shared memory beside the part's buffer, so the other threads never divide.
+struct ChunkSlot {
+    uint64_t lo, hi;
+    int64_t in_off, out_off;
+    int32_t my_first, last_first;
+};
+
+__device__ __forceinline__ int32_t clamp_first(int64_t f, int G) {
+    return (int32_t)max((int64_t)-1, min(f, (int64_t)G));
 }
 
-// Thread 0: start the bulk copy of CTA b's part of logical chunk c into its
-// buffer (full parts only; a ragged final part is read from global memory).
 template <typename T>
-__device__ __forceinline__ void chunk_stage_in(const ChunkParams<T> &p, int b, uint64_t c, T *buf, uint64_t *bar) {
-    uint64_t lo, hi;
-    chunk_part_range(p, b, c, lo, hi);
+__device__ __forceinline__ ChunkSlot chunk_slot(const ChunkParams<T> &p, int b, uint64_t c) {
+    ChunkSlot r{0, 0, 0, 0, (int32_t)gridDim.x, (int32_t)gridDim.x};
+    const uint64_t c0 = c * gridDim.x;
+    const uint64_t v = c0 + (uint64_t)b;
+    const bool one = p.lines == 1;  // one line: no division
+    const uint64_t last_line = one ? 0 : min((c0 + gridDim.x - 1) / p.ppl, p.lines - 1);
+    r.last_first = last_line == 0 ? -1 : clamp_first((int64_t)(last_line * p.ppl) - (int64_t)c0, gridDim.x);
+    if (v >= p.parts) return r;  // past the last line's last part
+    const uint64_t line = one ? 0 : v / p.ppl;
+    const uint64_t j = v - line * p.ppl;
+    const uint64_t jp = p.reverse ? p.ppl - 1 - j : j;
+    r.lo = jp * p.part;
+    r.hi = min(p.len, r.lo + p.part);
+    r.in_off = (int64_t)line * p.in_line;
+    r.out_off = (int64_t)line * p.out_line;
+    r.my_first = line == 0 ? -1 : clamp_first((int64_t)(line * p.ppl) - (int64_t)c0, gridDim.x);
+    return r;
+}
+
+// Thread 0: record CTA b's part of logical chunk c in its slot and start the
+// bulk copy of the part into its buffer (full parts only; a ragged part, the
+// last of a line, is read from global memory).
+template <typename T>
+__device__ __forceinline__ void chunk_stage_in(const ChunkParams<T> &p, int b, uint64_t c, T *buf, uint64_t *bar,
+                                               ChunkSlot *slots) {
+    const ChunkSlot r = chunk_slot(p, b, c);
     const int k = (int)(c % p.buffers);
-    if (hi - lo == p.part) bulk_load(buf + k * p.part, p.in + lo, (uint32_t)(p.part * sizeof(T)), &bar[k]);
+    slots[k] = r;
+    if (r.hi - r.lo == p.part)
+        bulk_load(buf + k * p.part, p.in + r.in_off + r.lo, (uint32_t)(p.part * sizeof(T)), &bar[k]);
 }
 
 
@@ -620,11 +665,11 @@ __device__ __forceinline__ void chunk_stage_in(const ChunkParams<T> &p, int b, u
 template <typename T, int OP, int JV, bool REV, int TPP>
 __device__ __forceinline__ void chunk_prescan_part(const ChunkParams<T> &p, int b, uint64_t c, const T *buf,
                                                    uint64_t *bar, uint32_t &phases, T (*s_warp)[kScanWarps],
-                                                   int &parity, T *s_red, TileScan<T, JV> (&rs)[TPP]) {
+                                                   int &parity, T *s_red, TileScan<T, JV> (&rs)[TPP],
+                                                   const ChunkSlot *slots) {
     constexpr int TILE = ScanShape<T, JV>::TILE;
-    uint64_t lo, hi;
-    chunk_part_range(p, b, c, lo, hi);
-    const uint64_t n = hi - lo;
+    const ChunkSlot pr = slots[c % p.buffers];
+    const uint64_t n = pr.hi - pr.lo;
     if (n == p.part) {
         const int k = (int)(c % p.buffers);
         mbar_wait(&bar[k], (phases >> k) & 1u, p.err);
@@ -646,7 +691,8 @@ __device__ __forceinline__ void chunk_prescan_part(const ChunkParams<T> &p, int 
     constexpr int V = Vec16<T>::V;
     (void)V;
     T acc = identity<T, OP>();
-    for (uint64_t e = lo + threadIdx.x; e < hi; e += kScanThreads) acc = combine<T, OP>(acc, p.in[e]);
+    const T *lin = p.in + pr.in_off;
+    for (uint64_t e = pr.lo + threadIdx.x; e < pr.hi; e += kScanThreads) acc = combine<T, OP>(acc, lin[e]);
     // One barrier, no trailing one: s_red is rewritten only by the next
     // ragged part, which cannot come before the next barriers.
     acc = warp_fold<T, OP>(acc);
@@ -673,6 +719,7 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
     __shared__ T s_warp[2][kScanWarps];
     __shared__ T s_red[kScanWarps];
     __shared__ T s_pair[2][kScanWarps];
+    __shared__ ChunkSlot s_slot[kChunkMaxBuffers];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int G = gridDim.x, b = blockIdx.x;
     const int NB = p.buffers;
@@ -684,7 +731,7 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
     if (threadIdx.x == 0) {
         for (int k = 0; k < NB; ++k) mbar_init(&bar[k], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int k = 0; k < NB && (uint64_t)k < p.nchunks; ++k) chunk_stage_in(p, b, k, buf, bar);
+        for (int k = 0; k < NB && (uint64_t)k < p.nchunks; ++k) chunk_stage_in(p, b, k, buf, bar, s_slot);
     }
     __syncthreads();
 
@@ -696,7 +743,7 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
 #pragma unroll
     for (int k = 0; k < L; ++k)
         if ((uint64_t)k < p.nchunks)
-            chunk_prescan_part<T, OP, JV, REV, TPP>(p, b, k, buf, bar, phases, s_warp, parity, s_red, ring[k]);
+            chunk_prescan_part<T, OP, JV, REV, TPP>(p, b, k, buf, bar, phases, s_warp, parity, s_red, ring[k], s_slot);
     for (uint64_t c = 0; c < p.nchunks; ++c) {
         // The part totals of chunk c were published one iteration ago: for
         // 4-byte T their status words are loaded here, before step 1, so the
@@ -716,10 +763,14 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
         }
         // Step 1: prescan of the part L chunks ahead, its total published.
         if (c + L < p.nchunks)
-            chunk_prescan_part<T, OP, JV, REV, TPP>(p, b, c + L, buf, bar, phases, s_warp, parity, s_red, ring[L]);
+            chunk_prescan_part<T, OP, JV, REV, TPP>(p, b, c + L, buf, bar, phases, s_warp, parity, s_red, ring[L], s_slot);
 
-        // Step 2: the part totals of chunk c.
-        T before = identity<T, OP>(), total = identity<T, OP>();
+        // Step 2: the part totals of chunk c.  `before` folds the parts of
+        // this CTA's line before its own in the chunk; `tail` folds the parts
+        // of the chunk's last line (the carry into the next chunk).
+        const ChunkSlot pr = s_slot[c % NB];  // read before thread 0 can restage the slot
+        const int32_t my_first = pr.my_first, last_first = pr.last_first;
+        T before = identity<T, OP>(), tail = identity<T, OP>();
 #pragma unroll
         for (int i = 0; i < kChunkMaxPartsPerThread; ++i) {
             const int q = threadIdx.x + i * kScanThreads;
@@ -743,31 +794,32 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
                 __nanosleep(32);
                 ok = read_status(p.status, c * G + q, v) != kStateInvalid;
             }
-            total = combine<T, OP>(total, v);
-            if (rev ? (q > b) : (q < b)) before = combine<T, OP>(before, v);
+            if (q >= last_first) tail = combine<T, OP>(tail, v);
+            if (q < b && q >= my_first) before = combine<T, OP>(before, v);
         }
         // Both folds share one barrier; s_pair is rewritten only in the next
         // iteration, after step 1's barriers.
         before = warp_fold<T, OP>(before);
-        total = warp_fold<T, OP>(total);
+        tail = warp_fold<T, OP>(tail);
         if (lane == 0) {
             s_pair[0][warp] = before;
-            s_pair[1][warp] = total;
+            s_pair[1][warp] = tail;
         }
         __syncthreads();
         before = s_pair[0][0];
-        total = s_pair[1][0];
+        tail = s_pair[1][0];
 #pragma unroll
         for (int w = 1; w < kScanWarps; ++w) {
             before = combine<T, OP>(before, s_pair[0][w]);
-            total = combine<T, OP>(total, s_pair[1][w]);
+            tail = combine<T, OP>(tail, s_pair[1][w]);
         }
-        T run = combine<T, OP>(carry, before);
-        carry = combine<T, OP>(carry, total);
+        T run = my_first < 0 ? combine<T, OP>(carry, before) : before;
+        carry = last_first < 0 ? combine<T, OP>(carry, tail) : tail;
 
         // Step 3: the part's outputs, tile by tile in logical order.
-        uint64_t lo, hi;
-        chunk_part_range(p, b, c, lo, hi);
+        const uint64_t lo = pr.lo, hi = pr.hi;
+        const T *lin = p.in + pr.in_off;
+        T *lout = p.out + pr.out_off;
         if (hi - lo == p.part) {
             // Staged and prescanned: reload, redo the in-vector scans, add
             // the prefixes.  No barrier.
@@ -783,14 +835,14 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
                     __syncthreads();
                     if (threadIdx.x == 0 && c + NB < p.nchunks) {
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                        chunk_stage_in(p, b, c + NB, buf, bar);
+                        chunk_stage_in(p, b, c + NB, buf, bar, s_slot);
                     }
                 }
                 vector_local_scan<T, OP, JV, REV>(x);
                 T y[JV][V];
                 tile_outputs<T, OP, JV, REV, EXCL>(x, ring[0][tp], run, y);
                 run = combine<T, OP>(run, ring[0][tp].agg);
-                store_tile<T, JV>(p.out + lo + (uint64_t)tp * TILE, TILE, true, base, y, p.store_mode);
+                store_tile<T, JV>(lout + lo + (uint64_t)tp * TILE, TILE, true, base, y, p.store_mode);
             }
         } else {
             const uint64_t ntiles = (hi - lo + TILE - 1) / TILE;
@@ -800,18 +852,18 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
                 const uint64_t valid = min((uint64_t)TILE, hi - lo - start);
                 const bool full = valid == (uint64_t)TILE;
                 T x[JV][V];
-                if (full) load_tile_vec<T, JV>(p.in + lo + start, base, x, false);
-                else load_tile_scalar<T, OP, JV>(p.in + lo + start, valid, base, x);
+                if (full) load_tile_vec<T, JV>(lin + lo + start, base, x, false);
+                else load_tile_scalar<T, OP, JV>(lin + lo + start, valid, base, x);
                 TileScan<T, JV> r;
                 tile_local_scan<T, OP, JV, REV>(x, s_warp[parity], r);
                 parity ^= 1;
                 T y[JV][V];
                 tile_outputs<T, OP, JV, REV, EXCL>(x, r, run, y);
                 run = combine<T, OP>(run, r.agg);
-                store_tile<T, JV>(p.out + lo + start, valid, full, base, y, p.store_mode);
+                store_tile<T, JV>(lout + lo + start, valid, full, base, y, p.store_mode);
             }
             // A ragged or empty part never used its buffer.
-            if (threadIdx.x == 0 && c + NB < p.nchunks) chunk_stage_in(p, b, c + NB, buf, bar);
+            if (threadIdx.x == 0 && c + NB < p.nchunks) chunk_stage_in(p, b, c + NB, buf, bar, s_slot);
         }
 #pragma unroll
         for (int k = 0; k < L; ++k)
@@ -879,11 +931,13 @@ static heph_status status_for(Device *dev, cudaStream_t stream, uint64_t entries
     return HEPH_OK;
 }
 
-// The chunked kernel for one long aligned line.  Returns false (nothing
-// launched) when the line is too short to give every CTA four parts.
+// The chunked kernel for `lines` aligned lines of `len` elements (line starts
+// in_line / out_line elements apart).  Returns false (nothing launched) when
+// the lines are too short to give every CTA four parts.
 template <typename T, int OP, bool REV, bool EXCL, int L, int TPP>
-static bool launch_chunked(Device *dev, cudaStream_t stream, const T *in, T *out, uint64_t len, bool reverse,
-                           bool exclusive, const T *carry, heph_status *st, int default_ctas) {
+static bool launch_chunked(Device *dev, cudaStream_t stream, const T *in, T *out, uint64_t len, uint64_t lines,
+                           int64_t in_line, int64_t out_line, bool reverse, bool exclusive, const T *carry,
+                           heph_status *st, int default_ctas) {
     using S = ScanShape<T, kChunkVectors>;
     const int nb = std::min(kChunkMaxBuffers, std::max(L + 2, scan_knob("HEPH_SCAN_BUFS", L + 2)));
     const uint64_t part = (uint64_t)TPP * S::TILE;
@@ -915,14 +969,19 @@ static bool launch_chunked(Device *dev, cudaStream_t stream, const T *in, T *out
     const int per_sm = std::min(nb_sm, std::max(1, scan_knob("HEPH_SCAN_CHUNK_CTAS", default_ctas)));
     const uint64_t G =
         std::min<uint64_t>((uint64_t)dev->sm_count * per_sm, (uint64_t)kChunkMaxPartsPerThread * kScanThreads);
-    if (len < 4 * part * G) return false;
+    const uint64_t ppl = (len + part - 1) / part;
+    if (lines == 0 || ppl * lines < 4 * G) return false;
     ChunkParams<T> cp{};
     cp.in = in;
     cp.out = out;
     cp.len = len;
+    cp.lines = lines;
+    cp.in_line = in_line;
+    cp.out_line = out_line;
+    cp.ppl = ppl;
+    cp.parts = ppl * lines;
     cp.part = part;
-    cp.chunk = part * G;
-    cp.nchunks = (len + cp.chunk - 1) / cp.chunk;
+    cp.nchunks = (ppl * lines + G - 1) / G;
     cp.carry = carry;
     cp.err = dev->error_dev;
     cp.reverse = reverse;
@@ -950,10 +1009,11 @@ constexpr int kChunkTilesPerPart = 1;
 constexpr int kChunkCtasPerSm = 3;
 
 template <typename T, int OP, bool REV, bool EXCL>
-static bool launch_chunked_any(Device *dev, cudaStream_t stream, const T *in, T *out, uint64_t len, bool reverse,
-                               bool exclusive, const T *carry, heph_status *st) {
-    return launch_chunked<T, OP, REV, EXCL, kChunkLookahead, kChunkTilesPerPart>(dev, stream, in, out, len, reverse,
-                                                                                exclusive, carry, st, kChunkCtasPerSm);
+static bool launch_chunked_any(Device *dev, cudaStream_t stream, const T *in, T *out, uint64_t len, uint64_t lines,
+                               int64_t in_line, int64_t out_line, bool reverse, bool exclusive, const T *carry,
+                               heph_status *st) {
+    return launch_chunked<T, OP, REV, EXCL, kChunkLookahead, kChunkTilesPerPart>(
+        dev, stream, in, out, len, lines, in_line, out_line, reverse, exclusive, carry, st, kChunkCtasPerSm);
 }
 
 template <typename T, int OP, int JV>
@@ -1020,29 +1080,24 @@ static heph_status launch_scan_typed(Device *dev, cudaStream_t stream, const T *
                      (pr.outer == 1 || (((uint64_t)pr.in_o * sizeof(T)) % 16 == 0 &&
                                         ((uint64_t)pr.out_o * sizeof(T)) % 16 == 0));
     std::lock_guard<std::mutex> lock(dev->mu);
-    // A line long enough for the chunked kernel takes it; of several lines,
-    // each of at least 128 MiB takes it with one launch per line (a few long
-    // lines would otherwise wait along their look-back chains; below that the
-    // chunked kernel's ~13 us of fixed cost per launch outweighs the gain:
-    // 4 x 2^26 u32 3.5 -> 5.3 TB/s, 16 x 2^24 3.6 -> 3.7, 3 x 7.5 M 3.1 ->
-    // 2.4).  Whether a line qualifies depends only on its length, so either
-    // every line is launched or none is.
-    const bool per_line = pr.outer == 1 || pr.len * sizeof(T) >= kPerLineChunkedBytes;
-    if (vec && per_line && !scan_knob("HEPH_SCAN_NO_CHUNKED", 0)) {
+    // One line long enough for the chunked kernel takes it; several lines
+    // take it too (one launch for all of them, each line's parts with their
+    // own running prefix) once every line spans kMultiLineChunkedBytes:
+    // along lines that long the look-back chains, not HBM, bound the
+    // look-back kernel.
+    const bool chunked_shape = pr.outer == 1 || pr.len * sizeof(T) >= (uint64_t)scan_knob_u64(
+                                                      "HEPH_SCAN_MULTI_CHUNKED_BYTES", kMultiLineChunkedBytes);
+    if (vec && chunked_shape && !scan_knob("HEPH_SCAN_NO_CHUNKED", 0)) {
         heph_status st = HEPH_OK;
-        bool launched = false;
-        for (uint64_t line = 0; line < pr.outer; ++line) {
-            const T *ci = in + pr.in_base + (int64_t)line * pr.in_o;
-            T *co = out + pr.out_base + (int64_t)line * pr.out_o;
-            const T *lc = line == 0 ? carry : nullptr;
-            if (reverse)
-                launched = exclusive ? launch_chunked_any<T, OP, true, true>(dev, stream, ci, co, pr.len, reverse, exclusive, lc, &st)
-                                     : launch_chunked_any<T, OP, true, false>(dev, stream, ci, co, pr.len, reverse, exclusive, lc, &st);
-            else
-                launched = exclusive ? launch_chunked_any<T, OP, false, true>(dev, stream, ci, co, pr.len, reverse, exclusive, lc, &st)
-                                     : launch_chunked_any<T, OP, false, false>(dev, stream, ci, co, pr.len, reverse, exclusive, lc, &st);
-            if (!launched || st != HEPH_OK) break;
-        }
+        const T *ci = in + pr.in_base;
+        T *co = out + pr.out_base;
+        bool launched;
+        if (reverse)
+            launched = exclusive ? launch_chunked_any<T, OP, true, true>(dev, stream, ci, co, pr.len, pr.outer, pr.in_o, pr.out_o, reverse, exclusive, carry, &st)
+                                 : launch_chunked_any<T, OP, true, false>(dev, stream, ci, co, pr.len, pr.outer, pr.in_o, pr.out_o, reverse, exclusive, carry, &st);
+        else
+            launched = exclusive ? launch_chunked_any<T, OP, false, true>(dev, stream, ci, co, pr.len, pr.outer, pr.in_o, pr.out_o, reverse, exclusive, carry, &st)
+                                 : launch_chunked_any<T, OP, false, false>(dev, stream, ci, co, pr.len, pr.outer, pr.in_o, pr.out_o, reverse, exclusive, carry, &st);
         if (launched) return st;
     }
     // A single line of 640+ tiles below the chunked kernel's minimum: the

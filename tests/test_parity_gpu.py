@@ -314,22 +314,63 @@ def test_scan_two_pass_lines(device, oracle, dt):
                 assert_close(device.download_owned(out), want[:n], dt, x[off:])
 
 
-@pytest.mark.parametrize("dt,shape", [(np.uint32, (2, 33_554_444)), (np.int64, (2, 16_777_220)),
-                                      (np.uint32, (3, 7_500_000))])
-def test_chunked_scan_multiline(device, oracle, dt, shape):
-    """Several lines of at least 128 MiB take the chunked kernel, one launch
-    per line: each line starts from the identity (no carry leaks from the line
-    before).  (3, 7.5 M) u32 lines qualify for it alone but take look-back."""
-    rng = np.random.default_rng(77)
-    x = rand(dt, shape[0] * shape[1], rng)
-    buf, out = device.upload(x), device.alloc_zeroed(dt, x.size)
+def _check_rows_scan(device, oracle, dt, shape, ld=None, op=CumSumOp, seed=77):
+    """Row scans (axis 1) of a [rows x cols] view with row stride `ld` into a
+    dense output, every direction / inclusive-exclusive pair, against the
+    oracle."""
+    rows, cols = shape
+    ld = ld or cols
+    rng = np.random.default_rng(seed)
+    x = rand(dt, rows * ld, rng, prod=op is CumProdOp)
+    buf, out = device.upload(x), device.alloc_zeroed(dt, rows * cols)
+    il, ol = Layout.try_new([rows, cols], [ld, 1], 0), Layout.c_contiguous([rows, cols])
     for rev in (False, True):
         for exc in (False, True):
-            CudaScanOps().scan_axis_into(CumSumOp, device, StridedView(buf, Layout.c_contiguous(list(shape))), 1,
-                                         int(rev), StridedView(out, Layout.c_contiguous(list(shape))), exclusive=exc)
-            np.testing.assert_array_equal(device.download_owned(out),
-                                          oracle.scan_axis(x, list(shape), 1, reverse=rev, exclusive=exc),
-                                          err_msg=f"rev={rev} exc={exc}")
+            CudaScanOps().scan_axis_into(op, device, StridedView(buf, il), 1, int(rev), StridedView(out, ol),
+                                         exclusive=exc)
+            want = oracle.scan_axis(x, [rows, cols], 1, op=1 if op is CumProdOp else 0, reverse=rev,
+                                    exclusive=exc, in_strides=[ld, 1])
+            got = device.download_owned(out)
+            if np.dtype(dt).kind == "f":
+                np.testing.assert_allclose(got.astype(np.float64), want.astype(np.float64), rtol=0,
+                                           atol=tol(dt, x), err_msg=f"rev={rev} exc={exc}")
+            else:
+                np.testing.assert_array_equal(got, want, err_msg=f"rev={rev} exc={exc}")
+    device.synchronize()  # no device-side error (wait timeout) was raised
+
+
+@pytest.mark.parametrize("dt,shape", [(np.uint32, (2, 33_554_444)), (np.int64, (2, 16_777_220)),
+                                      (np.uint32, (3, 7_500_000)), (np.uint32, (16, 1 << 21)),
+                                      (np.float32, (4, 3_000_020)), (np.int32, (64, 1 << 17))])
+def test_chunked_scan_multiline(device, oracle, dt, shape, monkeypatch):
+    """Several long lines take the chunked kernel in ONE launch: every line's
+    parts carry their own running prefix and each line starts from the
+    identity (nothing leaks from the line before).  Line lengths that the part
+    does not divide give every line a ragged last part.  The threshold knob is
+    lowered for the shorter shapes so that they take the kernel too."""
+    monkeypatch.setenv("HEPH_SCAN_MULTI_CHUNKED_BYTES", str(1 << 19))
+    _check_rows_scan(device, oracle, dt, shape)
+
+
+@pytest.mark.parametrize("dt,shape,ld", [(np.uint32, (5, 1_000_004), 1_000_008),
+                                         (np.int64, (40, 100_002), 100_004),
+                                         (np.uint32, (300, 20_000), 20_000),
+                                         (np.float64, (7, 700_002), 700_004)])
+def test_chunked_scan_multiline_many_chunks(device, oracle, dt, shape, ld, monkeypatch):
+    """One chunked CTA per SM (148 parts per chunk) and the threshold lowered:
+    lines begin and end in the middle of chunks, a line spans several chunks
+    or several lines share one, and the row stride differs from the row
+    length (input lines padded, output dense).  Rows stay 16-byte aligned
+    (the kernel's condition) while the part does not divide them."""
+    monkeypatch.setenv("HEPH_SCAN_CHUNK_CTAS", "1")
+    monkeypatch.setenv("HEPH_SCAN_MULTI_CHUNKED_BYTES", "1")
+    _check_rows_scan(device, oracle, dt, shape, ld=ld, seed=78)
+
+
+def test_chunked_scan_multiline_prod(device, oracle, monkeypatch):
+    monkeypatch.setenv("HEPH_SCAN_CHUNK_CTAS", "1")
+    monkeypatch.setenv("HEPH_SCAN_MULTI_CHUNKED_BYTES", "1")
+    _check_rows_scan(device, oracle, np.uint32, (9, 700_004), op=CumProdOp, seed=79)
 
 
 @pytest.fixture
