@@ -743,12 +743,23 @@ def main():
 
     latency = None
     if args.config == 1:
-        # Latency mode: one 4 MiB reduction on its own (reduce_dense_kernel),
-        # median of 20 event-timed calls over rotating buffers.  Each timed
-        # call is queued behind a ~50 us replay of the batch, so the events
-        # bracket the device's work and not the host's time to issue it.
-        ls, le = [], []
+        # Latency mode: single 4 MiB reductions (reduce_dense_kernel), each its
+        # own call over rotating buffers.  (a) back to back: 64 calls queued
+        # behind a spin, so the events time the device and not the host's
+        # issue: device time per call; (b) one call on its own, bracketed by
+        # events behind a replay of the batch (median of 20).
         with torch.cuda.stream(stream):
+            per_call = []
+            for rep in range(5):
+                torch.cuda._sleep(10_000_000)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for k in range(nbuf):
+                    ops.reduce_full_into(SumOp, dev, StridedView(bufs[k], lay),
+                                         StridedView(out, Layout.try_new([1], [1], k)), stream=sp)
+                b.record(stream)
+                per_call.append((a, b))
+            ls, le = [], []
             for k in range(23):
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 batch.launch(stream=sp)
@@ -759,8 +770,10 @@ def main():
                 ls.append(a)
                 le.append(b)
         dev.synchronize_stream(sp)
-        us = statistics.median(a.elapsed_time(b) * 1e3 for a, b in list(zip(ls, le))[3:])
-        latency = {"us_per_reduction": round(us, 3), "kernel": "reduce_dense_kernel",
+        us = statistics.median(a.elapsed_time(b) * 1e3 / nbuf for a, b in per_call)
+        single = statistics.median(a.elapsed_time(b) * 1e3 for a, b in list(zip(ls, le))[3:])
+        latency = {"us_per_reduction": round(us, 3), "mode": "64 separate calls back to back, per call",
+                   "single_call_us": round(single, 3), "kernel": "reduce_dense_kernel",
                    "gbs": round(4 * n / (us / 1e6) / 1e9, 2)}
 
     # ---------------- end to end through the public API with host buffers -------------
