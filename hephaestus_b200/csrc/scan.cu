@@ -622,34 +622,64 @@ __device__ __forceinline__ int32_t clamp_first(int64_t f, int G) {
     return (int32_t)max((int64_t)-1, min(f, (int64_t)G));
 }
 
+// Thread 0's position of the next chunk to stage: line and part-in-line of
+// this CTA's part (v = c*G + b) and of the chunk's last part (c*G + G - 1).
+// Chunks are staged in increasing order, so the cursor advances by G parts
+// with a subtraction or two instead of a 64-bit division per chunk (thread 0
+// stages in the middle of the output step, where extra latency delays the
+// whole CTA at its next barrier).
+struct PartCursor {
+    uint64_t line, j, last_line, last_j;
+};
+
+template <typename T> __device__ __forceinline__ PartCursor part_cursor_start(const ChunkParams<T> &p, int b) {
+    PartCursor q;
+    q.line = (uint64_t)b / p.ppl;
+    q.j = (uint64_t)b - q.line * p.ppl;
+    q.last_line = (uint64_t)(gridDim.x - 1) / p.ppl;
+    q.last_j = (uint64_t)(gridDim.x - 1) - q.last_line * p.ppl;
+    return q;
+}
+
+template <typename T> __device__ __forceinline__ void part_cursor_advance(const ChunkParams<T> &p, PartCursor &q) {
+    q.j += gridDim.x;
+    while (q.j >= p.ppl) {
+        q.j -= p.ppl;
+        ++q.line;
+    }
+    q.last_j += gridDim.x;
+    while (q.last_j >= p.ppl) {
+        q.last_j -= p.ppl;
+        ++q.last_line;
+    }
+}
+
 template <typename T>
-__device__ __forceinline__ ChunkSlot chunk_slot(const ChunkParams<T> &p, int b, uint64_t c) {
+__device__ __forceinline__ ChunkSlot chunk_slot(const ChunkParams<T> &p, uint64_t c, const PartCursor &q) {
     ChunkSlot r{0, 0, 0, 0, (int32_t)gridDim.x, (int32_t)gridDim.x};
     const uint64_t c0 = c * gridDim.x;
-    const uint64_t v = c0 + (uint64_t)b;
-    const bool one = p.lines == 1;  // one line: no division
-    const uint64_t last_line = one ? 0 : min((c0 + gridDim.x - 1) / p.ppl, p.lines - 1);
+    const uint64_t last_line = min(q.last_line, p.lines - 1);
     r.last_first = last_line == 0 ? -1 : clamp_first((int64_t)(last_line * p.ppl) - (int64_t)c0, gridDim.x);
-    if (v >= p.parts) return r;  // past the last line's last part
-    const uint64_t line = one ? 0 : v / p.ppl;
-    const uint64_t j = v - line * p.ppl;
-    const uint64_t jp = p.reverse ? p.ppl - 1 - j : j;
+    if (q.line >= p.lines) return r;  // past the last line's last part
+    const uint64_t jp = p.reverse ? p.ppl - 1 - q.j : q.j;
     r.lo = jp * p.part;
     r.hi = min(p.len, r.lo + p.part);
-    r.in_off = (int64_t)line * p.in_line;
-    r.out_off = (int64_t)line * p.out_line;
-    r.my_first = line == 0 ? -1 : clamp_first((int64_t)(line * p.ppl) - (int64_t)c0, gridDim.x);
+    r.in_off = (int64_t)q.line * p.in_line;
+    r.out_off = (int64_t)q.line * p.out_line;
+    r.my_first = q.line == 0 ? -1 : clamp_first((int64_t)(q.line * p.ppl) - (int64_t)c0, gridDim.x);
     return r;
 }
 
-// Thread 0: record CTA b's part of logical chunk c in its slot and start the
-// bulk copy of the part into its buffer (full parts only; a ragged part, the
-// last of a line, is read from global memory).
+// Thread 0: record CTA b's part of logical chunk c (the cursor's chunk) in
+// its slot, start the bulk copy of the part into its buffer (full parts only;
+// a ragged part, the last of a line, is read from global memory), and move the
+// cursor to chunk c + 1.
 template <typename T>
-__device__ __forceinline__ void chunk_stage_in(const ChunkParams<T> &p, int b, uint64_t c, T *buf, uint64_t *bar,
-                                               ChunkSlot *slots) {
-    const ChunkSlot r = chunk_slot(p, b, c);
-    const int k = (int)(c % p.buffers);
+__device__ __forceinline__ void chunk_stage_in(const ChunkParams<T> &p, uint32_t c, T *buf, uint64_t *bar,
+                                               ChunkSlot *slots, PartCursor &q) {
+    const ChunkSlot r = chunk_slot(p, c, q);
+    part_cursor_advance(p, q);
+    const uint32_t k = c % (uint32_t)p.buffers;
     slots[k] = r;
     if (r.hi - r.lo == p.part)
         bulk_load(buf + k * p.part, p.in + r.in_off + r.lo, (uint32_t)(p.part * sizeof(T)), &bar[k]);
@@ -668,10 +698,10 @@ __device__ __forceinline__ void chunk_prescan_part(const ChunkParams<T> &p, int 
                                                    int &parity, T *s_red, TileScan<T, JV> (&rs)[TPP],
                                                    const ChunkSlot *slots) {
     constexpr int TILE = ScanShape<T, JV>::TILE;
-    const ChunkSlot pr = slots[c % p.buffers];
+    const ChunkSlot pr = slots[(uint32_t)c % (uint32_t)p.buffers];
     const uint64_t n = pr.hi - pr.lo;
     if (n == p.part) {
-        const int k = (int)(c % p.buffers);
+        const int k = (int)((uint32_t)c % (uint32_t)p.buffers);
         mbar_wait(&bar[k], (phases >> k) & 1u, p.err);
         phases ^= 1u << k;
         const int base = tile_base_pos<T, JV>(threadIdx.x >> 5, threadIdx.x & 31);
@@ -727,11 +757,13 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
     const int base = tile_base_pos<T, JV>(warp, lane);
     uint32_t phases = 0;
     int parity = 0;
+    PartCursor cursor{};  // thread 0's: the next chunk to stage
+    if (threadIdx.x == 0) cursor = part_cursor_start(p, b);
 
     if (threadIdx.x == 0) {
         for (int k = 0; k < NB; ++k) mbar_init(&bar[k], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int k = 0; k < NB && (uint64_t)k < p.nchunks; ++k) chunk_stage_in(p, b, k, buf, bar, s_slot);
+        for (int k = 0; k < NB && (uint64_t)k < p.nchunks; ++k) chunk_stage_in(p, (uint32_t)k, buf, bar, s_slot, cursor);
     }
     __syncthreads();
 
@@ -768,7 +800,7 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
         // Step 2: the part totals of chunk c.  `before` folds the parts of
         // this CTA's line before its own in the chunk; `tail` folds the parts
         // of the chunk's last line (the carry into the next chunk).
-        const ChunkSlot pr = s_slot[c % NB];  // read before thread 0 can restage the slot
+        const ChunkSlot pr = s_slot[(uint32_t)c % (uint32_t)NB];  // read before thread 0 can restage the slot
         const int32_t my_first = pr.my_first, last_first = pr.last_first;
         T before = identity<T, OP>(), tail = identity<T, OP>();
 #pragma unroll
@@ -823,7 +855,7 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
         if (hi - lo == p.part) {
             // Staged and prescanned: reload, redo the in-vector scans, add
             // the prefixes.  No barrier.
-            const T *src = buf + (c % NB) * p.part;
+            const T *src = buf + ((uint32_t)c % (uint32_t)NB) * p.part;
 #pragma unroll
             for (int tl = 0; tl < TPP; ++tl) {
                 const int tp = rev ? TPP - 1 - tl : tl;
@@ -835,7 +867,7 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
                     __syncthreads();
                     if (threadIdx.x == 0 && c + NB < p.nchunks) {
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                        chunk_stage_in(p, b, c + NB, buf, bar, s_slot);
+                        chunk_stage_in(p, (uint32_t)(c + NB), buf, bar, s_slot, cursor);
                     }
                 }
                 vector_local_scan<T, OP, JV, REV>(x);
@@ -863,7 +895,7 @@ __global__ void __launch_bounds__(kScanThreads, 3) scan_chunked_kernel(const Chu
                 store_tile<T, JV>(lout + lo + start, valid, full, base, y, p.store_mode);
             }
             // A ragged or empty part never used its buffer.
-            if (threadIdx.x == 0 && c + NB < p.nchunks) chunk_stage_in(p, b, c + NB, buf, bar, s_slot);
+            if (threadIdx.x == 0 && c + NB < p.nchunks) chunk_stage_in(p, (uint32_t)(c + NB), buf, bar, s_slot, cursor);
         }
 #pragma unroll
         for (int k = 0; k < L; ++k)
