@@ -817,6 +817,7 @@ def main():
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * args.steps,
             **({"check": check_result["status"], "check_detail": check_result["detail"]} if check_result else {}),
+            **({"exchange": "peer memory (one kernel)" if comm.peer_exchange else "ncclAllGather"} if comm else {}),
         }
         print(json.dumps(line), flush=True)
     if comm:

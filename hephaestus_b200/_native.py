@@ -105,6 +105,7 @@ SIGNATURES = [
     ("heph_comm_init", _st, [_vp, ctypes.c_char_p, _i, _i, _pp]),
     ("heph_comm_destroy", _st, [_vp]),
     ("heph_comm_abort", _st, [_vp]),
+    ("heph_comm_peer_exchange", _st, [_vp, ctypes.POINTER(ctypes.c_int)]),
     ("heph_comm_wait", _st, [_vp, _vp, _u32]),
     ("heph_selftest_comm_wait_policy", _st, [_i, _u32, ctypes.POINTER(_i)]),
     ("heph_partitioned_reduce_full", _st, [_vp, _i, _vp, _lp, _vp, _lp, _vp]),

@@ -117,6 +117,8 @@ static heph_status check_device_error(Device *dev) {
         return fail(HEPH_DISPATCH_FAILED, "look-back timeout: a scan tile waited too long for its predecessor");
     if (e & DEVERR_BULK_TIMEOUT)
         return fail(HEPH_DISPATCH_FAILED, "bulk copy timeout: a scan part's input never arrived");
+    if (e & DEVERR_EXCHANGE_TIMEOUT)
+        return fail(HEPH_DISPATCH_FAILED, "exchange timeout: a peer rank's total never arrived");
     if (e) return fail(HEPH_DISPATCH_FAILED, "device reported error code " + std::to_string(e));
     return HEPH_OK;
 }

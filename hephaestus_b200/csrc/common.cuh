@@ -178,7 +178,7 @@ heph_status workspace_for(Device *device, cudaStream_t stream, size_t partial_by
                           size_t scan_status_bytes, Workspace **out);
 
 // Device-side error codes written to Device::error_dev.
-enum DeviceError : unsigned int { DEVERR_LOOKBACK_TIMEOUT = 1u, DEVERR_BULK_TIMEOUT = 2u };
+enum DeviceError : unsigned int { DEVERR_LOOKBACK_TIMEOUT = 1u, DEVERR_BULK_TIMEOUT = 2u, DEVERR_EXCHANGE_TIMEOUT = 4u };
 
 }  // namespace heph
 

@@ -16,18 +16,30 @@
 //           thread folds the carry and the global reduction, then the seeded
 //           scan: every rank moves 3 bytes-units per element, as one GPU does
 //           for the same pair, so the pair scales with the rank count.
+//           The exchange of this pair runs over peer memory instead of
+//           NCCL when every rank could map every other rank's mailbox: ONE
+//           32-thread kernel stores the rank's 16-byte pair into each peer's
+//           mailbox over NVLink (data, then a release store of the call's
+//           epoch as the flag), waits (bounded by the global timer) for every
+//           rank's flag in its own mailbox, and folds the carry and the
+//           global reduction — one launch in place of ncclAllGather plus the
+//           fold kernel.
 // NCCL is resolved at run time from the libnccl.so.2 already loaded into the
 // process (torch's), else from the loader path, so this library carries no
 // link-time NCCL dependency.
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <string>
 #include <thread>
+#include <vector>
 
 #include "comm_wait.h"
 #include "common.cuh"
+#include "device_utils.cuh"
 #include "kernels.h"
 #include "plan.h"
 
@@ -40,6 +52,8 @@ struct NcclApi {
     ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
     ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
@@ -63,11 +77,12 @@ NcclApi &nccl() {
         api.GetUniqueId = (decltype(api.GetUniqueId))sym("ncclGetUniqueId");
         api.CommInitRank = (decltype(api.CommInitRank))sym("ncclCommInitRank");
         api.AllGather = (decltype(api.AllGather))sym("ncclAllGather");
+        api.AllReduce = (decltype(api.AllReduce))sym("ncclAllReduce");
         api.CommDestroy = (decltype(api.CommDestroy))sym("ncclCommDestroy");
         api.CommAbort = (decltype(api.CommAbort))sym("ncclCommAbort");
         api.CommGetAsyncError = (decltype(api.CommGetAsyncError))sym("ncclCommGetAsyncError");
         api.GetErrorString = (decltype(api.GetErrorString))sym("ncclGetErrorString");
-        api.loaded = api.GetUniqueId && api.CommInitRank && api.AllGather && api.CommDestroy &&
+        api.loaded = api.GetUniqueId && api.CommInitRank && api.AllGather && api.AllReduce && api.CommDestroy &&
                      api.CommAbort && api.GetErrorString;
         if (!api.loaded) api.why = "libnccl.so.2 lacks a required symbol";
     });
@@ -135,6 +150,115 @@ heph_status launch_fold_pairs(cudaStream_t s, int op2, const void *pairs, int nr
     return HEPH_OK;
 }
 
+// Mailbox of a rank: 2 epoch parities x nranks entries of 32 bytes, entry r
+// = [rank r's 16-byte pair][flag: the epoch of the call that wrote it][pad].
+// Parity alternates per call, so a fast rank writing call e+1 never
+// overwrites an entry a slow rank still has to read for call e (a rank can
+// only reach call e+2 after every rank has published call e+1, i.e. after
+// every rank finished reading call e).
+constexpr int kMailboxEntry = 32;
+constexpr int kMaxP2PRanks = 32;
+
+__device__ __forceinline__ void st_relaxed_sys(unsigned char *p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_sys(unsigned char *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned char *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned char *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One warp: lane r (< nranks) publishes this rank's pair into rank r's
+// mailbox, then waits for rank r's pair in this rank's mailbox; lane 0 folds
+// carry (lower ranks' totals, OP1) and the global reduction (all partials,
+// OP2) in rank order.  A pair that never arrives within the wait deadline
+// raises the device error bit and counts as the identity.
+template <typename T, int OP1, typename Tacc, int OP2>
+__global__ void __launch_bounds__(32) exchange_pairs_kernel(const unsigned char *__restrict__ pair,
+                                                            unsigned char *const *__restrict__ boxes,
+                                                            unsigned char *mybox, int nranks, int rank,
+                                                            unsigned long long epoch, T *__restrict__ carry,
+                                                            Tacc *__restrict__ global, unsigned int *err) {
+    __shared__ unsigned long long s_pair[kMaxP2PRanks][2];
+    const int r = threadIdx.x;
+    const size_t par = (size_t)(epoch & 1ull) * nranks;
+    if (r < nranks) {
+        const unsigned long long a = reinterpret_cast<const unsigned long long *>(pair)[0];
+        const unsigned long long b = reinterpret_cast<const unsigned long long *>(pair)[1];
+        unsigned char *dst = boxes[r] + (par + rank) * kMailboxEntry;
+        st_relaxed_sys(dst, a);
+        st_relaxed_sys(dst + 8, b);
+        st_release_sys(dst + 16, epoch);
+    }
+    if (r < nranks) {
+        const unsigned char *src = mybox + (par + r) * kMailboxEntry;
+        WaitDeadline deadline;
+        bool ok = true;
+        while (ld_acquire_sys(src + 16) != epoch) {
+            if (deadline.expired()) {
+                raise_device_error(err, DEVERR_EXCHANGE_TIMEOUT);
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
+        }
+        if (ok) {
+            s_pair[r][0] = ld_relaxed_sys(src);
+            s_pair[r][1] = ld_relaxed_sys(src + 8);
+        } else {
+            const T ti = identity<T, OP1>();
+            const Tacc ai = identity<Tacc, OP2>();
+            s_pair[r][0] = 0;
+            s_pair[r][1] = 0;
+            memcpy(&s_pair[r][0], &ti, sizeof(T));
+            memcpy(&s_pair[r][1], &ai, sizeof(Tacc));
+        }
+    }
+    __syncwarp();
+    if (r == 0) {
+        T c = identity<T, OP1>();
+        Tacc g = identity<Tacc, OP2>();
+        for (int q = 0; q < nranks; ++q) {
+            T t;
+            Tacc v;
+            memcpy(&t, &s_pair[q][0], sizeof(T));
+            memcpy(&v, &s_pair[q][1], sizeof(Tacc));
+            if (q < rank) c = combine<T, OP1>(c, t);
+            g = combine<Tacc, OP2>(g, v);
+        }
+        *carry = c;
+        *global = g;
+    }
+}
+
+template <typename T, int OP1, typename Tacc>
+heph_status launch_exchange_pairs(cudaStream_t s, int op2, const void *pair, unsigned char *const *boxes,
+                                  unsigned char *mybox, int nranks, int rank, unsigned long long epoch, void *carry,
+                                  void *global, unsigned int *err) {
+    const unsigned char *pp = static_cast<const unsigned char *>(pair);
+    T *c = static_cast<T *>(carry);
+    Tacc *g = static_cast<Tacc *>(global);
+    switch (op2) {
+#define HEPH_X(OP2_) exchange_pairs_kernel<T, OP1, Tacc, OP2_><<<1, 32, 0, s>>>(pp, boxes, mybox, nranks, rank, epoch, c, g, err)
+        case OP_SUM: HEPH_X(OP_SUM); break;
+        case OP_PROD: HEPH_X(OP_PROD); break;
+        case OP_MIN: HEPH_X(OP_MIN); break;
+        case OP_MAX: HEPH_X(OP_MAX); break;
+#undef HEPH_X
+        default: return fail(HEPH_INVALID_CONFIGURATION, "full reduction supports sum, prod, min and max");
+    }
+    HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "pair exchange launch");
+    return HEPH_OK;
+}
+
 }  // namespace
 }  // namespace heph
 
@@ -149,7 +273,95 @@ struct heph_comm {
     void *scratch = nullptr;
     size_t pair_off = 0;
     bool aborted = false;
+    // Peer-memory exchange (all ranks or none): this rank's mailbox, every
+    // rank's mailbox as mapped here (device array), the IPC mappings to
+    // close, and the epoch of the next call.
+    bool p2p = false;
+    unsigned char *mailbox = nullptr;
+    unsigned char **boxes_dev = nullptr;
+    std::vector<void *> opened;
+    unsigned long long epoch = 0;
 };
+
+namespace {
+
+// Maps every peer's mailbox through CUDA IPC.  Collective: every rank calls it
+// and every rank ends with the same p2p decision (all-reduces of the per-rank
+// outcome, min), so no rank waits on a mailbox a peer never writes: first
+// every rank must have created its mailbox and handle, then every rank must
+// have opened every peer's handle.
+void setup_p2p(heph_comm *c, cudaStream_t s) {
+    NcclApi &api = nccl();
+    const int n = c->nranks;
+    c->epoch = 1;
+    if (n < 2 || n > kMaxP2PRanks) return;  // the same on every rank
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    unsigned char *xfer = nullptr;  // [my handle][all handles][flag]
+    if (cudaMalloc(&xfer, hb * (n + 1) + 16) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    int32_t *flag = reinterpret_cast<int32_t *>(xfer + hb * (n + 1));
+    auto agree = [&](int mine) {  // min over the ranks; 0 on any failure
+        int all = 0;
+        if (cudaMemcpy(flag, &mine, sizeof(int32_t), cudaMemcpyHostToDevice) == cudaSuccess &&
+            api.AllReduce(flag, flag, 1, ncclInt32, ncclMin, c->nccl, s) == ncclSuccess &&
+            cudaStreamSynchronize(s) == cudaSuccess &&
+            cudaMemcpy(&all, flag, sizeof(int32_t), cudaMemcpyDeviceToHost) == cudaSuccess)
+            return all;
+        cudaGetLastError();
+        return 0;
+    };
+    const char *e = getenv("HEPH_DIST_EXCHANGE");
+    int ok = !(e && std::string(e) == "nccl");
+    const size_t box_bytes = 2 * (size_t)n * kMailboxEntry;
+    if (ok) {
+        cudaIpcMemHandle_t h;
+        ok = cudaMalloc(&c->mailbox, box_bytes) == cudaSuccess && cudaMemset(c->mailbox, 0, box_bytes) == cudaSuccess &&
+             cudaMalloc(&c->boxes_dev, sizeof(void *) * n) == cudaSuccess &&
+             cudaIpcGetMemHandle(&h, c->mailbox) == cudaSuccess &&
+             cudaMemcpy(xfer, &h, hb, cudaMemcpyHostToDevice) == cudaSuccess;
+        cudaGetLastError();
+    }
+    if (agree(ok) == 1) {
+        std::vector<unsigned char> handles(hb * n);
+        ok = api.AllGather(xfer, xfer + hb, hb, ncclUint8, c->nccl, s) == ncclSuccess &&
+             cudaStreamSynchronize(s) == cudaSuccess &&
+             cudaMemcpy(handles.data(), xfer + hb, hb * n, cudaMemcpyDeviceToHost) == cudaSuccess;
+        std::vector<unsigned char *> boxes(n, nullptr);
+        for (int r = 0; r < n && ok; ++r) {
+            if (r == c->rank) {
+                boxes[r] = c->mailbox;
+                continue;
+            }
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, handles.data() + hb * r, hb);
+            void *p = nullptr;
+            if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                ok = 0;
+                break;
+            }
+            c->opened.push_back(p);
+            boxes[r] = static_cast<unsigned char *>(p);
+        }
+        if (ok) ok = cudaMemcpy(c->boxes_dev, boxes.data(), sizeof(void *) * n, cudaMemcpyHostToDevice) == cudaSuccess;
+        cudaGetLastError();
+        c->p2p = agree(ok) == 1;
+    }
+    cudaFree(xfer);
+}
+
+void teardown_p2p(heph_comm *c) {
+    for (void *p : c->opened) cudaIpcCloseMemHandle(p);
+    c->opened.clear();
+    if (c->boxes_dev) cudaFree(c->boxes_dev);
+    if (c->mailbox) cudaFree(c->mailbox);
+    c->boxes_dev = nullptr;
+    c->mailbox = nullptr;
+    c->p2p = false;
+}
+
+}  // namespace
 
 extern "C" heph_status heph_comm_unique_id(uint8_t id[HEPH_COMM_ID_BYTES]) {
     static_assert(sizeof(ncclUniqueId) == HEPH_COMM_ID_BYTES, "NCCL id size");
@@ -192,6 +404,7 @@ extern "C" heph_status heph_comm_init(heph_device *device, const uint8_t id[HEPH
         delete c;
         return fail(HEPH_ALLOCATION_FAILED, "communicator scratch allocation failed");
     }
+    setup_p2p(c, dev->stream);
     *out = c;
     return HEPH_OK;
 }
@@ -199,9 +412,17 @@ extern "C" heph_status heph_comm_init(heph_device *device, const uint8_t id[HEPH
 extern "C" heph_status heph_comm_destroy(heph_comm *comm) {
     if (!comm) return HEPH_OK;
     cudaSetDevice(comm->device->ordinal);
+    if (!comm->aborted) cudaDeviceSynchronize();  // no exchange in flight before the mappings go
+    teardown_p2p(comm);
     if (comm->nccl && !comm->aborted) nccl().CommDestroy(comm->nccl);
     if (comm->scratch) cudaFree(comm->scratch);
     delete comm;
+    return HEPH_OK;
+}
+
+extern "C" heph_status heph_comm_peer_exchange(const heph_comm *comm, int *out) {
+    if (!comm || !out) return fail(HEPH_INVALID_CONFIGURATION, "null argument");
+    *out = comm->p2p ? 1 : 0;
     return HEPH_OK;
 }
 
@@ -398,12 +619,25 @@ extern "C" heph_status heph_partitioned_scan_reduce(heph_comm *comm, heph_op sca
             st = launch_reduce_full(dev, s, reduce_op, bi->dtype, br->dtype, bi->ptr, *in_layout, count, pair + 8);
     }
     if (st != HEPH_OK) return st;
-    // 2. every rank's pair.
-    ncclResult_t r = nccl().AllGather(pair, gathered, 16, ncclUint8, comm->nccl, s);
-    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
-    // 3. carry (lower ranks' totals) and the global reduction (all partials).
+    // 2 + 3. every rank's pair, then carry (lower ranks' totals) and the
+    // global reduction (all partials): over peer memory in one kernel, or an
+    // NCCL all-gather and a fold kernel.
     void *gdst = static_cast<char *>(br->ptr) + reduce_layout->offset * dtype_size(br->dtype);
+    const unsigned long long epoch = comm->epoch++;
+    ncclResult_t r = ncclSuccess;
+    if (!comm->p2p) {
+        r = nccl().AllGather(pair, gathered, 16, ncclUint8, comm->nccl, s);
+        if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
+    }
     auto fold = [&]<typename T, typename Tacc>() -> heph_status {
+        if (comm->p2p) {
+            if (scan_op == HEPH_SUM)
+                return launch_exchange_pairs<T, OP_SUM, Tacc>(s, reduce_op, pair, comm->boxes_dev, comm->mailbox,
+                                                             comm->nranks, comm->rank, epoch, carry, gdst,
+                                                             dev->error_dev);
+            return launch_exchange_pairs<T, OP_PROD, Tacc>(s, reduce_op, pair, comm->boxes_dev, comm->mailbox,
+                                                          comm->nranks, comm->rank, epoch, carry, gdst, dev->error_dev);
+        }
         if (scan_op == HEPH_SUM)
             return launch_fold_pairs<T, OP_SUM, Tacc>(s, reduce_op, gathered, comm->nranks, comm->rank, carry, gdst);
         return launch_fold_pairs<T, OP_PROD, Tacc>(s, reduce_op, gathered, comm->nranks, comm->rank, carry, gdst);

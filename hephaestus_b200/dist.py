@@ -68,6 +68,14 @@ class Communicator:
                                                  reduce_output.buffer.handle, ctypes.byref(rl),
                                                  ctypes.c_void_p(stream) if stream else None))
 
+    @property
+    def peer_exchange(self) -> bool:
+        """True when scan_reduce_into exchanges over peer memory (one kernel)
+        instead of an NCCL all-gather; the same on every rank."""
+        v = ctypes.c_int(0)
+        check(N.lib.heph_comm_peer_exchange(self._h, ctypes.byref(v)))
+        return bool(v.value)
+
     def wait(self, timeout_s: float, stream=None):
         """Host-side deadline on the calls queued on `stream` (heph_comm_wait):
         returns once they finished; raises HephaestusError (DispatchFailed)

@@ -350,6 +350,13 @@ heph_status heph_comm_init(heph_device *device, const uint8_t id[HEPH_COMM_ID_BY
 heph_status heph_comm_destroy(heph_comm *comm);
 /* Aborts in-flight NCCL work (failure path: a peer is gone). */
 heph_status heph_comm_abort(heph_comm *comm);
+/* [EXT] *out = 1 when heph_partitioned_scan_reduce exchanges the ranks'
+ * (total, partial) pairs over peer memory (every rank mapped every other
+ * rank's mailbox through CUDA IPC at heph_comm_init; one kernel stores and
+ * waits, bounded by a 2 s device deadline that reports DispatchFailed
+ * "exchange timeout…"), 0 when it uses ncclAllGather (mapping failed on some
+ * rank, more than 32 ranks, or HEPH_DIST_EXCHANGE=nccl).  All ranks agree. */
+heph_status heph_comm_peer_exchange(const heph_comm *comm, int *out);
 
 /* [EXT] Host-side deadline on a partitioned call: waits until `stream` (NULL
  * = the device's stream) has finished the work queued on it, polling NCCL's

@@ -65,6 +65,8 @@ def main():
     rank, world = dist.get_rank(), dist.get_world_size()
     dev = H.CudaDevice(int(os.environ["LOCAL_RANK"]))
     comm = Communicator.from_torch(dev)
+    with open(os.path.join(out_dir, f"exchange_{rank}.txt"), "w") as fh:
+        fh.write("peer" if comm.peer_exchange else "nccl")
     if len(sys.argv) > 2 and sys.argv[2] == "large":
         check_large(out_dir, dev, comm, rank, world)
         dev.synchronize()

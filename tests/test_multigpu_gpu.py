@@ -13,18 +13,26 @@ pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def test_partitioned_scan_and_reduce(tmp_path, oracle):
+@pytest.mark.parametrize("exchange", ["default", "nccl"])
+def test_partitioned_scan_and_reduce(tmp_path, oracle, exchange):
+    """exchange = default: the fused scan + reduce exchanges over peer memory
+    (B200s on NVLink map each other's mailboxes); nccl: forced onto the NCCL
+    all-gather (HEPH_DIST_EXCHANGE=nccl)."""
     import torch
     world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs two or more GPUs")
     world = min(world, 8)
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    if exchange == "nccl":
+        env["HEPH_DIST_EXCHANGE"] = "nccl"
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
-           "--master-addr", "127.0.0.1", "--master-port", "29533",
+           "--master-addr", "127.0.0.1", "--master-port", "29533" if exchange == "default" else "29535",
            os.path.join(ROOT, "tests", "dist_worker.py"), str(tmp_path)]
     res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stderr[-3000:]
+    used = {(tmp_path / f"exchange_{r}.txt").read_text() for r in range(world)}
+    assert used == ({"nccl"} if exchange == "nccl" else {"peer"}), used
     cat = lambda name: np.concatenate([np.load(tmp_path / f"{name}_{r}.npy") for r in range(world)])  # noqa: E731
     xi, xu = cat("in_i32"), cat("in_u32")
     np.testing.assert_array_equal(xi, oracle.generate(oracle.GEN_I32_PM1000, 4, xi.size))
