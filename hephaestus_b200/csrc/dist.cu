@@ -177,6 +177,8 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned char
 }
 
 // One warp: lane r (< nranks) publishes this rank's pair into rank r's
+// mailbox (the partitioned reduction uses only the partial, the scan only
+// the total: the other output pointer is null)
 // mailbox, then waits for rank r's pair in this rank's mailbox; lane 0 folds
 // carry (lower ranks' totals, OP1) and the global reduction (all partials,
 // OP2) in rank order.  A pair that never arrives within the wait deadline
@@ -234,8 +236,8 @@ __global__ void __launch_bounds__(32) exchange_pairs_kernel(const unsigned char 
             if (q < rank) c = combine<T, OP1>(c, t);
             g = combine<Tacc, OP2>(g, v);
         }
-        *carry = c;
-        *global = g;
+        if (carry) *carry = c;
+        if (global) *global = g;
     }
 }
 
@@ -524,12 +526,24 @@ extern "C" heph_status heph_partitioned_reduce_full(heph_comm *comm, heph_op op,
     if (st != HEPH_OK) return st;
     cudaStream_t s = resolve_stream(dev, stream);
     char *scratch = static_cast<char *>(comm->scratch);
+    const size_t es = dtype_size(bo->dtype);
+    void *dst = static_cast<char *>(bo->ptr) + out_layout->offset * es;
+    if (comm->p2p) {
+        // The partial goes in the pair's second slot; one kernel exchanges
+        // and folds every rank's partial into `dst`.
+        char *pair = scratch + comm->pair_off;
+        st = launch_reduce_full(dev, s, op, bi->dtype, bo->dtype, bi->ptr, *in_layout, count, pair + 8);
+        if (st != HEPH_OK) return st;
+        const unsigned long long epoch = comm->epoch++;
+        return dispatch_dtype(bo->dtype, [&]<typename T>() {
+            return launch_exchange_pairs<T, OP_SUM, T>(s, op, pair, comm->boxes_dev, comm->mailbox, comm->nranks,
+                                                       comm->rank, epoch, nullptr, dst, dev->error_dev);
+        });
+    }
     st = launch_reduce_full(dev, s, op, bi->dtype, bo->dtype, bi->ptr, *in_layout, count, scratch);
     if (st != HEPH_OK) return st;
-    const size_t es = dtype_size(bo->dtype);
     ncclResult_t r = nccl().AllGather(scratch, scratch + 16, es, ncclUint8, comm->nccl, s);
     if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
-    void *dst = static_cast<char *>(bo->ptr) + out_layout->offset * es;
     return dispatch_dtype(bo->dtype, [&]<typename T>() {
         return launch_fold<T>(s, op, scratch + 16, comm->nranks, dst);
     });
@@ -558,6 +572,24 @@ extern "C" heph_status heph_partitioned_scan(heph_comm *comm, heph_op op, int ex
     char *scratch = static_cast<char *>(comm->scratch);
     const size_t es = dtype_size(bi->dtype);
     // 1. total of the local slice (the identity for an empty slice).
+    if (comm->p2p) {
+        // Exchanged over peer memory (the pair's first slot) and folded into
+        // the carry by one kernel.
+        char *pair = scratch + comm->pair_off;
+        st = launch_reduce_full(dev, s, op, bi->dtype, bi->dtype, bi->ptr, *in_layout, noop ? 0 : p.len, pair);
+        if (st != HEPH_OK) return st;
+        const unsigned long long epoch = comm->epoch++;
+        st = dispatch_dtype(bi->dtype, [&]<typename T>() {
+            if (op == HEPH_SUM)
+                return launch_exchange_pairs<T, OP_SUM, T>(s, OP_SUM, pair, comm->boxes_dev, comm->mailbox,
+                                                           comm->nranks, comm->rank, epoch, scratch + 8, nullptr,
+                                                           dev->error_dev);
+            return launch_exchange_pairs<T, OP_PROD, T>(s, OP_SUM, pair, comm->boxes_dev, comm->mailbox, comm->nranks,
+                                                        comm->rank, epoch, scratch + 8, nullptr, dev->error_dev);
+        });
+        if (st != HEPH_OK || noop) return st;
+        return launch_scan(dev, s, op, bi->dtype, bi->ptr, bo->ptr, p, false, exclusive != 0, scratch + 8);
+    }
     st = launch_reduce_full(dev, s, op, bi->dtype, bi->dtype, bi->ptr, *in_layout, noop ? 0 : p.len, scratch);
     if (st != HEPH_OK) return st;
     // 2. every rank's total.

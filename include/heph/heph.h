@@ -350,8 +350,8 @@ heph_status heph_comm_init(heph_device *device, const uint8_t id[HEPH_COMM_ID_BY
 heph_status heph_comm_destroy(heph_comm *comm);
 /* Aborts in-flight NCCL work (failure path: a peer is gone). */
 heph_status heph_comm_abort(heph_comm *comm);
-/* [EXT] *out = 1 when heph_partitioned_scan_reduce exchanges the ranks'
- * (total, partial) pairs over peer memory (every rank mapped every other
+/* [EXT] *out = 1 when the partitioned calls exchange the ranks' totals /
+ * partials over peer memory (every rank mapped every other
  * rank's mailbox through CUDA IPC at heph_comm_init; one kernel stores and
  * waits, bounded by a 2 s device deadline that reports DispatchFailed
  * "exchange timeout…"), 0 when it uses ncclAllGather (mapping failed on some
@@ -378,16 +378,17 @@ heph_status heph_selftest_comm_wait_policy(int scenario, uint32_t timeout_ms, in
 /* Each rank holds one contiguous slice of a global 1-D buffer (rank order =
  * slice order).  `out` (one element, dtype may widen I32->I64 / F32->F64)
  * receives the reduction of the WHOLE global buffer on every rank: local
- * single-pass reduction, then one NCCL all-gather of the per-rank partials,
- * then a fixed-order combine on the device.  op: SUM, PROD, MIN, MAX. */
+ * single-pass reduction, then the exchange of the per-rank partials (over
+ * peer memory, or one NCCL all-gather: heph_comm_peer_exchange), then a
+ * fixed-order combine on the device.  op: SUM, PROD, MIN, MAX. */
 heph_status heph_partitioned_reduce_full(heph_comm *comm, heph_op op,
                                          const heph_buffer *in, const heph_layout *in_layout,
                                          heph_buffer *out, const heph_layout *out_layout,
                                          heph_stream stream);
 /* Forward scan of the global buffer: each rank writes its slice of the
  * global (inclusive or exclusive) prefix.  Reduce-then-scan: local total,
- * NCCL all-gather of the totals, carry = fold of the lower ranks' totals,
- * then the single-pass look-back scan seeded with that carry. */
+ * exchange of the totals (peer memory or NCCL all-gather), carry = fold of
+ * the lower ranks' totals, then the slice's scan seeded with that carry. */
 heph_status heph_partitioned_scan(heph_comm *comm, heph_op op, int exclusive,
                                   const heph_buffer *in, const heph_layout *in_layout,
                                   heph_buffer *out, const heph_layout *out_layout,
@@ -396,7 +397,7 @@ heph_status heph_partitioned_scan(heph_comm *comm, heph_op op, int exclusive,
  * buffer in one call (no counterpart in the reference): one local pass
  * computes the slice's scan total (scan_op: SUM, PROD) and its reduction
  * partial (reduce_op: SUM, PROD, MIN, MAX; reduce_out may widen I32->I64 /
- * F32->F64), one all-gather carries both, then the seeded scan.  Each rank
+ * F32->F64), one exchange carries both, then the seeded scan.  Each rank
  * reads its slice twice and writes it once - the traffic of the same pair of
  * calls on one GPU - instead of three reads.  Outputs must not alias the
  * input. */
