@@ -179,4 +179,39 @@ __device__ __forceinline__ void raise_device_error(unsigned int *err, unsigned i
     if (err) atomicOr(err, code);
 }
 
+// ------------------------------------------- bulk copies into shared memory
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// Thread 0: expect `bytes` on `bar` and start a bulk global->shared copy
+// (a plain bulk copy; the source is this GPU's own memory).
+__device__ __forceinline__ void bulk_load(void *dst_smem, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst_smem)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
+// Waits for phase `parity` of `bar`.  Bounded in time (WaitDeadline): past
+// the deadline the device error bit is raised and the wait gives up.
+__device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, unsigned int *err) {
+    WaitDeadline deadline;
+    while (true) {
+        uint32_t done;
+        asm volatile("{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n selp.u32 %0, 1, 0, P;\n}"
+                     : "=r"(done)
+                     : "r"(smem_addr(bar)), "r"(parity)
+                     : "memory");
+        if (done) return;
+        if (deadline.expired()) break;
+    }
+    if (threadIdx.x == 0) raise_device_error(err, DEVERR_BULK_TIMEOUT);
+}
+
 }  // namespace heph

@@ -129,6 +129,98 @@ __global__ void __launch_bounds__(kReduceThreads)
     finish_grid<Tacc, OP>(acc, out, partials, ticket, scratch);
 }
 
+// Large dense reductions staged through shared memory by bulk copies (TMA,
+// no multicast): each CTA keeps kBulkStages copies of 16 KiB in flight, so
+// the bytes in flight per SM are set by shared memory, not by registers;
+// CTA b folds 16 KiB blocks b, b + G, b + 2G, ...  The unaligned head and the
+// ragged tail are folded with plain loads by the whole grid.
+constexpr int kBulkStages = 6;
+constexpr uint32_t kBulkBlockBytes = 16384;
+constexpr int kBulkCtasPerSm = 2;
+constexpr uint64_t kBulkMinBytes = 256ull << 20;
+
+// This CTA's share of a dense run through the shared-memory stages: calls
+// fv(uint4) for every 16-byte vector of its 16 KiB blocks and fo(Tin) for
+// its elements of the head and the tail.
+template <typename Tin, typename FV, typename FO>
+__device__ __forceinline__ void bulk_stream(const Tin *__restrict__ in, uint64_t n, unsigned int *err,
+                                            unsigned char *stage, uint64_t *bar, FV &&fv, FO &&fo) {
+    constexpr uint64_t BE = kBulkBlockBytes / sizeof(Tin);
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(in);
+    uint64_t head = ((16u - (addr & 15u)) & 15u) / sizeof(Tin);
+    if (head > n) head = n;
+    const uint64_t nblocks = (n - head) / BE;
+    const Tin *body = in + head;
+    const uint64_t tail0 = head + nblocks * BE;
+    const uint64_t G = gridDim.x, b = blockIdx.x;
+    const uint64_t mine = nblocks > b ? (nblocks - b + G - 1) / G : 0;
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < kBulkStages; ++k) mbar_init(&bar[k], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (uint64_t k = 0; k < (uint64_t)kBulkStages && k < mine; ++k)
+            bulk_load(stage + k * kBulkBlockBytes, body + (b + k * G) * BE, kBulkBlockBytes, &bar[k]);
+    }
+    __syncthreads();
+    constexpr int U = kBulkBlockBytes / 16 / kReduceThreads;  // 16-byte vectors per thread per block
+    for (uint64_t i = 0; i < mine; ++i) {
+        const int k = (int)(i % kBulkStages);
+        mbar_wait(&bar[k], (uint32_t)((i / kBulkStages) & 1u), err);
+        const uint4 *src = reinterpret_cast<const uint4 *>(stage + k * kBulkBlockBytes);
+        uint4 r[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) r[u] = src[threadIdx.x + u * kReduceThreads];
+        __syncthreads();  // every thread has read stage k: refill it
+        if (threadIdx.x == 0 && i + kBulkStages < mine) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            bulk_load(stage + k * kBulkBlockBytes, body + (b + (i + kBulkStages) * G) * BE, kBulkBlockBytes, &bar[k]);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) fv(r[u]);
+    }
+    const uint64_t tid = b * kReduceThreads + threadIdx.x;
+    if (tid < head) fo(in[tid]);
+    for (uint64_t e = tail0 + tid; e < n; e += G * kReduceThreads) fo(in[e]);
+}
+
+// Dense runs of kBulkMinBytes and more stream through the shared-memory
+// stages (i32 -> i64 sum of 2^32 elements: 6736 -> 7176 GB/s; 1 GiB of f32 the
+// same either way; a 64 MiB f32 sum, partly in L2, slower: 6958 -> 6072).
+// HEPH_REDUCE_BULK_MIN (bytes, read once) moves the threshold; 0 turns the
+// bulk kernels off.
+static bool use_bulk(uint64_t bytes) {
+    static const uint64_t bulk_min = [] {
+        const char *e = getenv("HEPH_REDUCE_BULK_MIN");
+        return e ? strtoull(e, nullptr, 10) : kBulkMinBytes;
+    }();
+    return bulk_min && bytes >= bulk_min;
+}
+
+// Raises a kernel's dynamic shared-memory limit to the bulk stages, once per
+// (kernel, device ordinal); the caller holds the device's lock.
+template <typename K> static heph_status bulk_attr(K kernel, int ordinal) {
+    static bool set[64] = {};
+    if (ordinal >= 0 && ordinal < 64 && set[ordinal]) return HEPH_OK;
+    HEPH_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)(kBulkStages * kBulkBlockBytes)),
+                  HEPH_DISPATCH_FAILED, "bulk reduction attribute");
+    if (ordinal >= 0 && ordinal < 64) set[ordinal] = true;
+    return HEPH_OK;
+}
+
+template <typename Tin, typename Tacc, int OP>
+__global__ void __launch_bounds__(kReduceThreads, kBulkCtasPerSm)
+    reduce_bulk_kernel(const Tin *__restrict__ in, uint64_t n, Tacc *__restrict__ out, Tacc *__restrict__ partials,
+                       unsigned int *__restrict__ ticket, unsigned int *err) {
+    extern __shared__ __align__(128) unsigned char stage[];  // kBulkStages x 16 KiB
+    __shared__ uint64_t bar[kBulkStages];
+    __shared__ Tacc scratch[kReduceThreads / 32];
+    Tacc acc = identity<Tacc, OP>();
+    bulk_stream<Tin>(
+        in, n, err, stage, bar, [&](uint4 v) { acc = fold_vec<Tin, Tacc, OP>(acc, v); },
+        [&](Tin v) { acc = combine<Tacc, OP>(acc, (Tacc)v); });
+    finish_grid<Tacc, OP>(acc, out, partials, ticket, scratch);
+}
+
 // A fused batch of dense full reductions in one launch: problem p owns CTAs
 // [cta_begin, cta_begin + ctas) of the grid, its own partial slots (indexed
 // like its CTAs) and ticket.  A CTA finds its problem with one parallel read
@@ -319,6 +411,17 @@ static heph_status launch_typed(Device *dev, cudaStream_t stream, const void *ba
         // for its results in griddepcontrol.wait, which hides most of the
         // launch latency of back-to-back small reductions (2^20 f32 per call
         // 6.2 -> 4.4 us measured).  HEPH_REDUCE_PDL=0 turns it off.
+        if (use_bulk(count * sizeof(Tin))) {
+            auto kernel = reduce_bulk_kernel<Tin, Tacc, OP>;
+            const size_t smem = (size_t)kBulkStages * kBulkBlockBytes;
+            st = bulk_attr(kernel, dev->ordinal);
+            if (st != HEPH_OK) return st;
+            const unsigned bg = (unsigned)std::min<uint64_t>((uint64_t)dev->sm_count * kBulkCtasPerSm, (uint64_t)grid);
+            kernel<<<bg, kReduceThreads, smem, stream>>>(base + (dense ? (int64_t)l.offset : first), count, out, partials,
+                                                        ws->tickets, dev->error_dev);
+            HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "full reduction launch");
+            return HEPH_OK;
+        }
         static const bool pdl = [] {
             const char *e = getenv("HEPH_REDUCE_PDL");
             return !e || atoi(e) != 0;
@@ -388,10 +491,11 @@ heph_status launch_reduce_full(Device *dev, cudaStream_t stream, int op, heph_dt
 // Two reductions of one dense run in one read: op1 in T (e.g. the total a
 // partitioned scan needs for its carry) and op2 in Tacc (e.g. a widening sum
 // of the same slice).  Per-CTA partials of both, last-CTA finalize of both.
-template <typename Tin, int OP1, typename Tacc, int OP2>
+template <typename Tin, int OP1, typename Tacc, int OP2, bool BULK>
 __global__ void __launch_bounds__(kReduceThreads)
     reduce_dual_kernel(const Tin *__restrict__ in, uint64_t n, Tin *__restrict__ out1, Tacc *__restrict__ out2,
-                       Tin *__restrict__ partials1, Tacc *__restrict__ partials2, unsigned int *__restrict__ ticket) {
+                       Tin *__restrict__ partials1, Tacc *__restrict__ partials2, unsigned int *__restrict__ ticket,
+                       unsigned int *err) {
     __shared__ Tin scratch1[kReduceThreads / 32];
     __shared__ Tacc scratch2[kReduceThreads / 32];
     constexpr int V = Vec16<Tin>::V;
@@ -413,21 +517,28 @@ __global__ void __launch_bounds__(kReduceThreads)
             a2 = combine<Tacc, OP2>(a2, (Tacc)e.e[c]);
         }
     };
-    uint64_t i = tid;
-    for (; i + (kReduceUnroll - 1) * stride < nvec; i += kReduceUnroll * stride) {
-        uint4 r[kReduceUnroll];
-#pragma unroll
-        for (int u = 0; u < kReduceUnroll; ++u) r[u] = ld_stream(vin + i + u * stride);
-#pragma unroll
-        for (int u = 0; u < kReduceUnroll; ++u) fold(r[u]);
-    }
-    for (; i < nvec; i += stride) fold(ld_stream(vin + i));
     auto fold_one = [&](Tin v) {
         a1 = combine<Tin, OP1>(a1, v);
         a2 = combine<Tacc, OP2>(a2, (Tacc)v);
     };
-    if (tid < head) fold_one(in[tid]);
-    if (tid < n - tail) fold_one(in[tail + tid]);
+    if constexpr (BULK) {
+        extern __shared__ __align__(128) unsigned char stage[];  // kBulkStages x 16 KiB
+        __shared__ uint64_t bar[kBulkStages];
+        bulk_stream<Tin>(in, n, err, stage, bar, fold, fold_one);
+    } else {
+        (void)err;
+        uint64_t i = tid;
+        for (; i + (kReduceUnroll - 1) * stride < nvec; i += kReduceUnroll * stride) {
+            uint4 r[kReduceUnroll];
+#pragma unroll
+            for (int u = 0; u < kReduceUnroll; ++u) r[u] = ld_stream(vin + i + u * stride);
+#pragma unroll
+            for (int u = 0; u < kReduceUnroll; ++u) fold(r[u]);
+        }
+        for (; i < nvec; i += stride) fold(ld_stream(vin + i));
+        if (tid < head) fold_one(in[tid]);
+        if (tid < n - tail) fold_one(in[tail + tid]);
+    }
 
     a1 = block_fold<Tin, OP1, kReduceThreads>(a1, scratch1);
     a2 = block_fold<Tacc, OP2, kReduceThreads>(a2, scratch2);
@@ -477,13 +588,28 @@ static heph_status launch_dual_typed(Device *dev, cudaStream_t stream, int op2, 
     Tin *p1 = reinterpret_cast<Tin *>(static_cast<char *>(ws->partials) + (size_t)grid * sizeof(Tacc));
     Tin *o1 = static_cast<Tin *>(out1);
     Tacc *o2 = static_cast<Tacc *>(out2);
+    auto go = [&]<int OP2>() -> heph_status {
+        if (use_bulk(n * sizeof(Tin))) {
+            auto kernel = reduce_dual_kernel<Tin, OP1, Tacc, OP2, true>;
+            heph_status s2 = bulk_attr(kernel, dev->ordinal);
+            if (s2 != HEPH_OK) return s2;
+            const unsigned bg = (unsigned)std::min<uint64_t>((uint64_t)dev->sm_count * kBulkCtasPerSm, grid);
+            kernel<<<bg, kReduceThreads, (size_t)kBulkStages * kBulkBlockBytes, stream>>>(in, n, o1, o2, p1, p2,
+                                                                                          ws->tickets, dev->error_dev);
+        } else {
+            reduce_dual_kernel<Tin, OP1, Tacc, OP2, false><<<grid, kReduceThreads, 0, stream>>>(in, n, o1, o2, p1, p2,
+                                                                                               ws->tickets, nullptr);
+        }
+        return HEPH_OK;
+    };
     switch (op2) {
-        case OP_SUM: reduce_dual_kernel<Tin, OP1, Tacc, OP_SUM><<<grid, kReduceThreads, 0, stream>>>(in, n, o1, o2, p1, p2, ws->tickets); break;
-        case OP_PROD: reduce_dual_kernel<Tin, OP1, Tacc, OP_PROD><<<grid, kReduceThreads, 0, stream>>>(in, n, o1, o2, p1, p2, ws->tickets); break;
-        case OP_MIN: reduce_dual_kernel<Tin, OP1, Tacc, OP_MIN><<<grid, kReduceThreads, 0, stream>>>(in, n, o1, o2, p1, p2, ws->tickets); break;
-        case OP_MAX: reduce_dual_kernel<Tin, OP1, Tacc, OP_MAX><<<grid, kReduceThreads, 0, stream>>>(in, n, o1, o2, p1, p2, ws->tickets); break;
+        case OP_SUM: st = go.template operator()<OP_SUM>(); break;
+        case OP_PROD: st = go.template operator()<OP_PROD>(); break;
+        case OP_MIN: st = go.template operator()<OP_MIN>(); break;
+        case OP_MAX: st = go.template operator()<OP_MAX>(); break;
         default: return fail(HEPH_INVALID_CONFIGURATION, "full reduction supports sum, prod, min and max");
     }
+    if (st != HEPH_OK) return st;
     HEPH_CUDA_TRY(cudaGetLastError(), HEPH_DISPATCH_FAILED, "dual reduction launch");
     return HEPH_OK;
 }

@@ -797,3 +797,29 @@ def test_misaligned_arg_reductions_with_ties(device, oracle, dt, op):
             wv, wi = oracle.arg_reduce_axis(x, lay.shape, axis, op=op, in_strides=lay.strides, in_offset=lay.offset)
             np.testing.assert_array_equal(device.download_owned(idx), wi, err_msg=str(lay))
             np.testing.assert_array_equal(device.download_owned(vals), wv)
+
+
+@pytest.mark.parametrize("dt,op,acc,n,off", [(np.float32, SumOp, np.float32, (1 << 26) + 5, 1),
+                                            (np.int32, SumOp, np.int64, (1 << 26) + 1029, 3),
+                                            (np.uint32, MaxOp, np.uint32, (1 << 26) + 4096, 0),
+                                            (np.float64, MinOp, np.float64, (1 << 25) + 7, 1)])
+def test_full_reduction_bulk_staged(device, oracle, dt, op, acc, n, off):
+    """Dense runs of 256 MiB and more stream through shared-memory stages
+    filled by bulk copies: a 16-byte-misaligned head, whole 16 KiB blocks
+    spread over the grid, a ragged tail."""
+    import hephaestus_b200.seams as S
+    kind = {np.dtype(np.float32): S.SYNTH_F32_UNIFORM_PM1, np.dtype(np.int32): S.SYNTH_I32_PM1000,
+            np.dtype(np.uint32): S.SYNTH_U32_LOW4, np.dtype(np.float64): S.SYNTH_F64_UNIT}[np.dtype(dt)]
+    x = device.alloc_uninitialized(dt, n + off)
+    S.synth_fill(device, x, kind, seed=11)
+    out = device.alloc_zeroed(acc, 1)
+    for _ in range(2):
+        CudaFullReductionOps().reduce_full_into(op, device, StridedView(x, Layout.try_new([n], [1], off)),
+                                                StridedView(out, Layout.c_contiguous([1])))
+        got = device.download_owned(out)[0]
+        hx = device.download_owned(x)[off:]
+        want = oracle.reduce_full(np.ascontiguousarray(hx), [n], op=op.code, out_dtype=acc)
+        if np.dtype(acc).kind == "f" and op is SumOp:
+            assert abs(float(got) - float(want)) <= tol(dt, hx)
+        else:
+            assert got == want
