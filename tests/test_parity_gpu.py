@@ -823,3 +823,37 @@ def test_full_reduction_bulk_staged(device, oracle, dt, op, acc, n, off):
             assert abs(float(got) - float(want)) <= tol(dt, hx)
         else:
             assert got == want
+
+
+@pytest.mark.parametrize("dt,acc", [(np.float32, np.float32), (np.int32, np.int64), (np.uint32, np.uint32)])
+def test_fused_batch_large(device, oracle, dt, acc):
+    """A fused batch of more than 256 MiB: problems of very different sizes
+    (many CTAs each, or one), misaligned starts, ragged tails, replayed three
+    times."""
+    import hephaestus_b200.seams as S
+    kind = {np.dtype(np.float32): S.SYNTH_F32_UNIFORM_PM1, np.dtype(np.int32): S.SYNTH_I32_PM1000,
+            np.dtype(np.uint32): S.SYNTH_U32_LOW4}[np.dtype(dt)]
+    sizes, offs = [(1 << 24) + 3, (1 << 25) + 7, 5, 1 << 24, 30_000_001, 70_001], [1, 0, 2, 0, 3, 1]
+    bufs = []
+    for k, (n, off) in enumerate(zip(sizes, offs)):
+        b = device.alloc_uninitialized(dt, n + off)
+        S.synth_fill(device, b, kind, seed=20 + k)
+        bufs.append(b)
+    out = device.alloc_zeroed(acc, len(sizes))
+    ops = CudaFullReductionOps()
+    items = [ops.prepare_reduce_full(SumOp, device, StridedView(b, Layout.try_new([n], [1], off)),
+                                     StridedView(out, Layout.try_new([1], [1], k)))
+             for k, (b, n, off) in enumerate(zip(bufs, sizes, offs))]
+    hx = [device.download_owned(b)[off:] for b, off in zip(bufs, offs)]
+    want = [oracle.reduce_full(np.ascontiguousarray(x), [x.size], out_dtype=acc) for x in hx]
+    batch = S.Batch(device, items)
+    for _ in range(3):
+        device.write_buffer(out, np.zeros(len(sizes), dtype=acc))
+        batch.launch()
+        got = device.download_owned(out)
+        for k, x in enumerate(hx):
+            if np.dtype(acc).kind == "f":
+                assert abs(float(got[k]) - float(want[k])) <= tol(dt, x), k
+            else:
+                assert got[k] == want[k], k
+    device.synchronize()
