@@ -70,6 +70,9 @@ CONFIGS = {
     # A few long lines: all of them in one launch of the chunked kernel.
     9: dict(workload="u32 inclusive scan along the rows (axis 1) of a [16 x 2^24] row-major matrix, "
                      "h&15 seed 1", rows=16, cols=1 << 24, dtype="u32", kernel="scan_chunked_kernel"),
+    # One large dense full reduction (the shared-memory-staged kernel).
+    10: dict(workload="f32 full sum reduction over 2^28 elements (1 GiB), uniform[-1,1) seed 0",
+             n=1 << 28, dtype="f32", kernel="reduce_bulk_kernel", bytes_per_elem=4),
 }
 
 
@@ -210,7 +213,7 @@ def cpu_workload(cfg_id: int, cfg: dict, oracle, threads: int):
             oracle.inclusive_scan_i32_mt(x, out, 0, threads)
             oracle.sum_i32_to_i64_mt(x, threads)
         return step5, 12 * n, f"i32 inclusive scan + i64 sum of {n} elements ({mt})"
-    if cfg_id == 1:
+    if cfg_id in (1, 10):
         n = cfg["n"]
         x = data(("x", 1, n), lambda: oracle.generate(oracle.GEN_F32_UNIFORM_PM1, 0, n))
         return (lambda: oracle.sum_f32_mt(x, threads)), 4 * n, f"f32 sum of {n} elements ({mt})"
@@ -626,6 +629,21 @@ def main():
         launches_per_step = 2  # column slices + slice finalize
         kernel_step = None
         units = rows * cols
+    elif args.config == 10:
+        n = cfg["n"]
+        x = dev.alloc_uninitialized(np.float32, n)
+        S.synth_fill(dev, x, S.SYNTH_F32_UNIFORM_PM1, seed=0, stream=sp)
+        out = dev.alloc_zeroed(np.float32, 1)
+        ops = H.CudaFullReductionOps()
+        lay10 = Layout.c_contiguous([n])
+
+        def step():
+            ops.reduce_full_into(SumOp, dev, StridedView(x, lay10), StridedView(out, Layout.c_contiguous([1])),
+                                 stream=sp)
+        bytes_per_step = 4 * n
+        kernel_bytes = bytes_per_step
+        kernel_step = None
+        units = n
     elif args.config in (6, 7):
         rows, cols, ld, off = cfg["rows"], cfg["cols"], cfg["ld"], cfg["offset"]
         x = dev.alloc_uninitialized(np.float32, rows * ld + off)
@@ -944,7 +962,7 @@ def run_e2e(args, cfg, dev, stream, sp, world, rank, comm, max_over_ranks, barri
                 check(N.lib.heph_buffer_download_async(dev.handle, y.handle, 0, hout, n, ctypes.c_void_p(sp)))
                 check(N.lib.heph_buffer_download_async(dev.handle, s64.handle, 0, hsum, 1, ctypes.c_void_p(sp)))
         bytes_step, h2d, d2h = 12 * n, 4 * n, 4 * n + 8
-    elif args.config == 1:
+    elif args.config in (1, 10):
         n = cfg["n"]
         hin = pinned(4 * n)
         hout = pinned(4)
