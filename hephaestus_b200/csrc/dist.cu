@@ -30,6 +30,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -356,6 +357,26 @@ void setup_p2p(heph_comm *c, cudaStream_t s) {
 void teardown_p2p(heph_comm *c) {
     for (void *p : c->opened) cudaIpcCloseMemHandle(p);
     c->opened.clear();
+    if (c->p2p && !c->aborted) {
+        // Every rank has closed its mappings of the others' mailboxes before
+        // any rank frees its own: a one-element all-reduce as the barrier,
+        // waited for at most 5 s (a rank that is gone aborts the NCCL
+        // communicator instead of hanging the teardown).
+        int32_t *flag = reinterpret_cast<int32_t *>(c->mailbox);
+        cudaStream_t s = c->device->stream;
+        if (nccl().AllReduce(flag, flag, 1, ncclInt32, ncclMax, c->nccl, s) == ncclSuccess) {
+            const auto t0 = std::chrono::steady_clock::now();
+            while (cudaStreamQuery(s) == cudaErrorNotReady) {
+                if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(5)) {
+                    nccl().CommAbort(c->nccl);
+                    c->aborted = true;
+                    break;
+                }
+                std::this_thread::sleep_for(std::chrono::microseconds(100));
+            }
+        }
+        cudaGetLastError();
+    }
     if (c->boxes_dev) cudaFree(c->boxes_dev);
     if (c->mailbox) cudaFree(c->mailbox);
     c->boxes_dev = nullptr;
