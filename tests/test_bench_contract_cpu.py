@@ -41,3 +41,20 @@ def test_reference_arm_other_ranks_print_nothing():
     res = run_reference({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert res.returncode == 0, res.stderr[-2000:]
     assert res.stdout.strip() == ""
+
+
+def test_both_arms_build_the_same_config():
+    """The GPU arm and the reference arm print the same `config` object for
+    the same flags (both call bench.config_dict), at every world size."""
+    import argparse
+    sys.path.insert(0, ROOT)
+    import bench
+    res = run_reference({"WORLD_SIZE": "4", "RANK": "0", "LOCAL_RANK": "0"})
+    assert res.returncode == 0, res.stderr[-2000:]
+    ref = json.loads(res.stdout.strip().splitlines()[-1])["config"]
+    args = argparse.Namespace(config=2, partitioned=False)
+    assert ref == bench.config_dict(args, dict(bench.CONFIGS[2]), 4)
+    for world in (1, 2, 8):
+        c5 = bench.config_dict(argparse.Namespace(config=5, partitioned=False), dict(bench.CONFIGS[5]), world)
+        assert c5["elements_total"] == 1 << 32 and c5["elements_per_gpu"] == (1 << 32) // world
+        assert c5["parallelism"] == ("single" if world == 1 else f"partitioned1d{world}")
